@@ -1,0 +1,579 @@
+// api.inl — the extern "C" entry points of libcpq (host code).
+//
+// Validation happens here, on the host, before anything is launched: every
+// shape, stride, alignment and type outside the fast path returns a status
+// (CPQ_ERR_UNSUPPORTED / CPQ_ERR_INVALID_ARG) instead of aborting, where
+// ggml would GGML_ASSERT (docs/BENCHMARKS.md:199-203 notes such aborts).
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+#include <string>
+
+namespace cpq {
+
+static thread_local std::string g_last_error;
+
+static cpq_status fail(cpq_status s, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return s;
+}
+
+static cpq_status cuda_fail(cudaError_t e, const char *what) {
+    return fail(CPQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+constexpr int kMaxDevices = 64;
+
+struct DevState {
+    void *ws = nullptr;
+    size_t ws_bytes = 0;
+};
+static std::mutex g_mu;
+static DevState g_dev[kMaxDevices];
+
+static int sm_count(int dev) {
+    static std::atomic<int> cache[kMaxDevices];
+    int v = cache[dev].load(std::memory_order_relaxed);
+    if (v == 0) {
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        if (v <= 0) v = 1;
+        cache[dev].store(v, std::memory_order_relaxed);
+    }
+    return v;
+}
+
+static bool pdl_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("CPQ_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// Every kernel is launched with programmatic stream serialization allowed,
+// so its prologue can overlap the tail of the previous kernel on the stream;
+// each kernel calls griddepcontrol.wait before touching its inputs.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                          Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+static int current_device() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess) return -1;
+    return d;
+}
+
+// ---- type helpers -----------------------------------------------------------
+
+static int64_t type_blck(int32_t t) {
+    switch (t) {
+    case CPQ_TYPE_Q8_0: return kQK8_0;
+    case CPQ_TYPE_Q4_K:
+    case CPQ_TYPE_Q6_K:
+    case CPQ_TYPE_Q8_K: return kQK_K;
+    case CPQ_TYPE_F32:
+    case CPQ_TYPE_F16: return 1;
+    default: return 0;
+    }
+}
+
+static int64_t type_bytes(int32_t t) {
+    switch (t) {
+    case CPQ_TYPE_Q8_0: return kQ8_0_Bytes;
+    case CPQ_TYPE_Q4_K: return kQ4K_Bytes;
+    case CPQ_TYPE_Q6_K: return kQ6K_Bytes;
+    case CPQ_TYPE_Q8_K: return kQ8K_Bytes;
+    case CPQ_TYPE_F32: return 4;
+    case CPQ_TYPE_F16: return 2;
+    default: return 0;
+    }
+}
+
+// ggml-cpu's vec_dot_type for each weight type on this path.
+static int32_t vec_dot_type(int32_t wt) {
+    switch (wt) {
+    case CPQ_TYPE_Q4_K:
+    case CPQ_TYPE_Q6_K: return CPQ_TYPE_Q8_K;
+    case CPQ_TYPE_Q8_0: return CPQ_TYPE_Q8_0;
+    default: return -1;
+    }
+}
+
+static const char *type_name(int32_t t) {
+    switch (t) {
+    case CPQ_TYPE_F32: return "F32";
+    case CPQ_TYPE_F16: return "F16";
+    case CPQ_TYPE_Q8_0: return "Q8_0";
+    case CPQ_TYPE_Q4_K: return "Q4_K";
+    case CPQ_TYPE_Q6_K: return "Q6_K";
+    case CPQ_TYPE_Q8_K: return "Q8_K";
+    default: return "unknown";
+    }
+}
+
+static bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ---- validation ------------------------------------------------------------
+
+struct MMShape {
+    int32_t wtype;
+    int64_t k, n, m;
+};
+
+static cpq_status check_weight(const cpq_tensor *w, MMShape *s) {
+    if (!w) return fail(CPQ_ERR_INVALID_ARG, "weight descriptor is null");
+    if (vec_dot_type(w->type) < 0)
+        return fail(CPQ_ERR_UNSUPPORTED, "weight type %s (%d) is not Q4_K, Q6_K or Q8_0", type_name(w->type), w->type);
+    if (w->ne[2] != 1 || w->ne[3] != 1)
+        return fail(CPQ_ERR_UNSUPPORTED, "weight ne[2]=%lld ne[3]=%lld: only 2-D weights", (long long)w->ne[2],
+                    (long long)w->ne[3]);
+    const int64_t blk = type_blck(w->type), bb = type_bytes(w->type);
+    if (w->ne[0] <= 0 || w->ne[1] < 0) return fail(CPQ_ERR_INVALID_ARG, "weight ne[0]=%lld ne[1]=%lld", (long long)w->ne[0], (long long)w->ne[1]);
+    if (w->ne[0] % blk != 0)
+        return fail(CPQ_ERR_INVALID_ARG, "weight ne[0]=%lld is not a multiple of the %s block (%lld)",
+                    (long long)w->ne[0], type_name(w->type), (long long)blk);
+    const size_t row = size_t(w->ne[0] / blk) * size_t(bb);
+    if (w->nb[0] != size_t(bb)) return fail(CPQ_ERR_UNSUPPORTED, "weight nb[0]=%zu != block size %lld", w->nb[0], (long long)bb);
+    if (w->nb[1] < row) return fail(CPQ_ERR_INVALID_ARG, "weight nb[1]=%zu < row size %zu", w->nb[1], row);
+    if (w->type == CPQ_TYPE_Q4_K && w->nb[1] % 16 != 0)
+        return fail(CPQ_ERR_UNSUPPORTED, "Q4_K row stride %zu is not a multiple of 16 bytes", w->nb[1]);
+    if (w->nb[1] % 2 != 0) return fail(CPQ_ERR_UNSUPPORTED, "weight row stride %zu is odd", w->nb[1]);
+    if (w->ne[1] > 0 && !w->data) return fail(CPQ_ERR_INVALID_ARG, "weight data is null");
+    if (!aligned(w->data, 16)) return fail(CPQ_ERR_UNSUPPORTED, "weight data is not 16-byte aligned");
+    s->wtype = w->type;
+    s->k = w->ne[0];
+    s->n = w->ne[1];
+    return CPQ_SUCCESS;
+}
+
+static cpq_status check_x(const cpq_tensor *x, int64_t k, int64_t *m) {
+    if (!x) return fail(CPQ_ERR_INVALID_ARG, "activation descriptor is null");
+    if (x->type != CPQ_TYPE_F32) return fail(CPQ_ERR_UNSUPPORTED, "activation type %s: only F32", type_name(x->type));
+    if (x->ne[2] != 1 || x->ne[3] != 1) return fail(CPQ_ERR_UNSUPPORTED, "activation must be 2-D");
+    if (x->ne[0] != k)
+        return fail(CPQ_ERR_INVALID_ARG, "activation ne[0]=%lld != weight ne[0]=%lld", (long long)x->ne[0], (long long)k);
+    if (x->ne[1] < 0) return fail(CPQ_ERR_INVALID_ARG, "activation ne[1] < 0");
+    if (x->nb[0] != 4) return fail(CPQ_ERR_UNSUPPORTED, "activation nb[0]=%zu: rows must be contiguous", x->nb[0]);
+    if (x->nb[1] < size_t(k) * 4 || x->nb[1] % 16 != 0)
+        return fail(CPQ_ERR_UNSUPPORTED, "activation nb[1]=%zu must be >= 4*K and a multiple of 16", x->nb[1]);
+    if (x->ne[1] > 0 && (!x->data || !aligned(x->data, 16)))
+        return fail(CPQ_ERR_UNSUPPORTED, "activation data null or not 16-byte aligned");
+    *m = x->ne[1];
+    return CPQ_SUCCESS;
+}
+
+static cpq_status check_y(const cpq_tensor *y, int64_t n, int64_t m) {
+    if (!y) return fail(CPQ_ERR_INVALID_ARG, "output descriptor is null");
+    if (y->type != CPQ_TYPE_F32) return fail(CPQ_ERR_UNSUPPORTED, "output type %s: only F32", type_name(y->type));
+    if (y->ne[2] != 1 || y->ne[3] != 1) return fail(CPQ_ERR_UNSUPPORTED, "output must be 2-D");
+    if (y->ne[0] != n || y->ne[1] != m)
+        return fail(CPQ_ERR_INVALID_ARG, "output ne=[%lld,%lld], expected [%lld,%lld]", (long long)y->ne[0],
+                    (long long)y->ne[1], (long long)n, (long long)m);
+    if (y->nb[0] != 4 || y->nb[1] < size_t(n) * 4 || y->nb[1] % 4 != 0)
+        return fail(CPQ_ERR_UNSUPPORTED, "output strides nb[0]=%zu nb[1]=%zu", y->nb[0], y->nb[1]);
+    if (n > 0 && m > 0 && (!y->data || !aligned(y->data, 4))) return fail(CPQ_ERR_INVALID_ARG, "output data null or misaligned");
+    return CPQ_SUCCESS;
+}
+
+// ---- launches -----------------------------------------------------------------
+
+static cudaError_t launch_quantize(int32_t vt, const float *x, int64_t k, int64_t m, int64_t x_stride, void *ws,
+                                   const ActLayout &L, uint8_t *aos, cudaStream_t st) {
+    int8_t *qs = ws ? reinterpret_cast<int8_t *>(static_cast<uint8_t *>(ws) + L.qs_off) : nullptr;
+    float *d = ws ? reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + L.d_off) : nullptr;
+    int16_t *bs = ws ? reinterpret_cast<int16_t *>(static_cast<uint8_t *>(ws) + L.bs_off) : nullptr;
+    if (vt == CPQ_TYPE_Q8_K) {
+        const int64_t blocks = m * (k / kQK_K);  // one warp each, 8 per CTA
+        const int64_t grid = std::min<int64_t>((blocks + 7) / 8, 65535);
+        return launch(quantize_q8K_kernel, dim3(unsigned(grid)), dim3(256), 0, st, x, k, m, x_stride, qs, d, bs, aos);
+    }
+    const int64_t blocks = m * (k / kQK8_0);  // 4 lanes each, 64 per CTA
+    const int64_t grid = std::min<int64_t>((blocks + 63) / 64, 65535);
+    return launch(quantize_q8_0_kernel, dim3(unsigned(grid)), dim3(256), 0, st, x, k, m, x_stride, qs, d, aos);
+}
+
+template <class F, int MT>
+static cudaError_t launch_gemv_t(const GemvArgs &a, cudaStream_t st) {
+    constexpr int smem = GemvSmem<F>::kBytes;
+    auto kern = gemv_kernel<F, MT>;
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    static std::atomic<int> occ[kMaxDevices];
+    int bpm = occ[dev].load(std::memory_order_relaxed);
+    if (bpm == 0) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bpm, kern, kGemvWarps * 32, smem);
+        if (e != cudaSuccess) return e;
+        if (bpm < 1) bpm = 1;
+        occ[dev].store(bpm, std::memory_order_relaxed);
+    }
+    const int64_t ntot = a.row_start[a.n_w];
+    const int64_t want = (ntot + kGemvWarps - 1) / kGemvWarps;
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(want, int64_t(sm_count(dev)) * bpm));
+    return launch(kern, dim3(unsigned(grid)), dim3(kGemvWarps * 32), smem, st, a);
+}
+
+template <class F>
+static cudaError_t launch_gemv(const GemvArgs &a, int mt, cudaStream_t st) {
+    switch (mt) {
+    case 1: return launch_gemv_t<F, 1>(a, st);
+    case 2: return launch_gemv_t<F, 2>(a, st);
+    case 3: return launch_gemv_t<F, 3>(a, st);
+    case 4: return launch_gemv_t<F, 4>(a, st);
+    case 5: return launch_gemv_t<F, 5>(a, st);
+    case 6: return launch_gemv_t<F, 6>(a, st);
+    case 7: return launch_gemv_t<F, 7>(a, st);
+    case 8: return launch_gemv_t<F, 8>(a, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+constexpr int kGemvMaxTokens = 8;  // tokens per GEMV launch
+
+// Quantize X once into the workspace, then run every weight against it.
+static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
+                               void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (n_w < 1 || n_w > kMaxMulti) return fail(CPQ_ERR_INVALID_ARG, "n_w=%d must be in 1..%d", n_w, kMaxMulti);
+    if (!w || !y) return fail(CPQ_ERR_INVALID_ARG, "weight/output arrays are null");
+    MMShape s0;
+    cpq_status rc = check_weight(w[0], &s0);
+    if (rc) return rc;
+    int64_t m = 0;
+    if ((rc = check_x(x, s0.k, &m))) return rc;
+    GemvArgs a = {};
+    a.n_w = n_w;
+    a.k = s0.k;
+    a.rs = w[0]->nb[1];
+    a.row_start[0] = 0;
+    for (int i = 0; i < n_w; i++) {
+        MMShape si;
+        if ((rc = check_weight(w[i], &si))) return rc;
+        if (si.wtype != s0.wtype || si.k != s0.k || w[i]->nb[1] != w[0]->nb[1])
+            return fail(CPQ_ERR_INVALID_ARG, "weights sharing an input must have one type, K and row stride");
+        if ((rc = check_y(y[i], si.n, m))) return rc;
+        a.w[i] = static_cast<const uint8_t *>(w[i]->data);
+        a.w_end[i] = si.n > 0 ? a.w[i] + size_t(si.n - 1) * w[i]->nb[1] + size_t(si.k / type_blck(si.wtype)) * type_bytes(si.wtype) : a.w[i];
+        a.y[i] = static_cast<float *>(y[i]->data);
+        a.y_stride[i] = int64_t(y[i]->nb[1] / 4);
+        a.row_start[i + 1] = a.row_start[i] + si.n;
+    }
+    if (m == 0 || a.row_start[n_w] == 0) return CPQ_SUCCESS;  // empty product: nothing to launch
+    const int32_t vt = vec_dot_type(s0.wtype);
+    const ActLayout L = act_layout(vt, s0.k, m);
+    if (!ws) return fail(CPQ_ERR_NOT_INITIALIZED, "no workspace (call cpq_init on this device first)");
+    if (ws_bytes < L.bytes) return fail(CPQ_ERR_WORKSPACE, "workspace %zu B < %zu B needed", ws_bytes, L.bytes);
+    if (!aligned(ws, 256)) return fail(CPQ_ERR_INVALID_ARG, "workspace must be 256-byte aligned");
+
+    cudaError_t e = launch_quantize(vt, static_cast<const float *>(x->data), s0.k, m, int64_t(x->nb[1] / 4), ws, L,
+                                    nullptr, st);
+    if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+
+    const uint8_t *base = static_cast<const uint8_t *>(ws);
+    const int64_t blk = type_blck(vt);
+    for (int64_t t0 = 0; t0 < m; t0 += kGemvMaxTokens) {
+        const int mt = int(std::min<int64_t>(kGemvMaxTokens, m - t0));
+        GemvArgs g = a;
+        g.act.qs = reinterpret_cast<const int8_t *>(base + L.qs_off) + t0 * s0.k;
+        g.act.d = reinterpret_cast<const float *>(base + L.d_off) + t0 * (s0.k / blk);
+        g.act.bsums = reinterpret_cast<const int16_t *>(base + L.bs_off) + t0 * (s0.k / 16);
+        for (int i = 0; i < n_w; i++) g.y[i] = a.y[i] + t0 * a.y_stride[i];
+        switch (s0.wtype) {
+        case CPQ_TYPE_Q4_K: e = launch_gemv<FmtQ4K>(g, mt, st); break;
+        case CPQ_TYPE_Q6_K: e = launch_gemv<FmtQ6K>(g, mt, st); break;
+        default: e = launch_gemv<FmtQ8_0>(g, mt, st); break;
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+    }
+    return CPQ_SUCCESS;
+}
+
+static cpq_status workspace_of_current(void **ws, size_t *bytes) {
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return fail(CPQ_ERR_CUDA, "no current CUDA device");
+    std::lock_guard<std::mutex> lk(g_mu);
+    *ws = g_dev[dev].ws;
+    *bytes = g_dev[dev].ws_bytes;
+    if (!*ws) return fail(CPQ_ERR_NOT_INITIALIZED, "cpq_init was not called for device %d", dev);
+    return CPQ_SUCCESS;
+}
+
+static int64_t grid_1d(int64_t n, int threads) {
+    return std::max<int64_t>(1, std::min<int64_t>((n + threads - 1) / threads, 4096));
+}
+
+}  // namespace cpq
+
+using namespace cpq;
+
+extern "C" {
+
+int cpq_abi_version(void) { return CPQ_ABI_VERSION; }
+
+const char *cpq_last_error(void) { return g_last_error.c_str(); }
+
+const char *cpq_status_string(cpq_status s) {
+    switch (s) {
+    case CPQ_SUCCESS: return "success";
+    case CPQ_ERR_INVALID_ARG: return "invalid argument";
+    case CPQ_ERR_UNSUPPORTED: return "unsupported";
+    case CPQ_ERR_NOT_INITIALIZED: return "not initialized";
+    case CPQ_ERR_WORKSPACE: return "workspace too small";
+    case CPQ_ERR_CUDA: return "CUDA error";
+    case CPQ_ERR_NCCL: return "NCCL error";
+    case CPQ_ERR_DEVICE: return "device-side error";
+    default: return "unknown status";
+    }
+}
+
+cpq_status cpq_init(int device, size_t workspace_bytes) {
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= ndev || device >= kMaxDevices) return fail(CPQ_ERR_INVALID_ARG, "device %d out of range", device);
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevState &ds = g_dev[device];
+    if (ds.ws && ds.ws_bytes >= workspace_bytes) return CPQ_SUCCESS;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    if (ds.ws) {
+        cudaDeviceSynchronize();
+        cudaFree(ds.ws);
+        ds.ws = nullptr;
+        ds.ws_bytes = 0;
+    }
+    const size_t bytes = std::max<size_t>(workspace_bytes, 256);
+    e = cudaMalloc(&ds.ws, bytes);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        ds.ws = nullptr;
+        return cuda_fail(e, "cudaMalloc(workspace)");
+    }
+    ds.ws_bytes = bytes;
+    return CPQ_SUCCESS;
+}
+
+cpq_status cpq_release(int device) {
+    if (device < 0 || device >= kMaxDevices) return fail(CPQ_ERR_INVALID_ARG, "device %d out of range", device);
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevState &ds = g_dev[device];
+    if (!ds.ws) return CPQ_SUCCESS;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    cudaDeviceSynchronize();
+    cudaError_t e = cudaFree(ds.ws);
+    cudaSetDevice(prev);
+    ds.ws = nullptr;
+    ds.ws_bytes = 0;
+    return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "cudaFree(workspace)");
+}
+
+size_t cpq_mul_mat_workspace_size(const cpq_tensor *w, const cpq_tensor *x) {
+    if (!w || !x) return 0;
+    const int32_t vt = vec_dot_type(w->type);
+    if (vt < 0 || x->ne[1] < 0 || w->ne[0] <= 0) return 0;
+    return act_layout(vt, w->ne[0], std::max<int64_t>(x->ne[1], 1)).bytes;
+}
+
+cpq_status cpq_mul_mat_ws(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *y, void *workspace,
+                          size_t workspace_bytes, void *stream) {
+    return mul_mat_core(&w, &y, 1, x, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+cpq_status cpq_mul_mat(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *y, void *stream) {
+    void *ws;
+    size_t bytes;
+    cpq_status rc = workspace_of_current(&ws, &bytes);
+    if (rc) return rc;
+    return mul_mat_core(&w, &y, 1, x, ws, bytes, static_cast<cudaStream_t>(stream));
+}
+
+cpq_status cpq_mul_mat_multi(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
+                             void *stream) {
+    void *ws;
+    size_t bytes;
+    cpq_status rc = workspace_of_current(&ws, &bytes);
+    if (rc) return rc;
+    return mul_mat_core(w, y, n_w, x, ws, bytes, static_cast<cudaStream_t>(stream));
+}
+
+cpq_status cpq_quantize_act(int32_t wtype, const float *x, void *out, int64_t k, int64_t m, void *stream) {
+    const int32_t vt = vec_dot_type(wtype);
+    if (vt < 0) return fail(CPQ_ERR_UNSUPPORTED, "weight type %s has no quantized vec_dot_type here", type_name(wtype));
+    if (k <= 0 || m < 0 || k % type_blck(vt) != 0)
+        return fail(CPQ_ERR_INVALID_ARG, "k=%lld must be a positive multiple of %lld", (long long)k, (long long)type_blck(vt));
+    if (m == 0) return CPQ_SUCCESS;
+    if (!x || !out || !aligned(x, 16)) return fail(CPQ_ERR_INVALID_ARG, "x/out null or x not 16-byte aligned");
+    if (!aligned(out, 4)) return fail(CPQ_ERR_INVALID_ARG, "out must be 4-byte aligned");
+    const ActLayout L = act_layout(vt, k, m);
+    cudaError_t e = launch_quantize(vt, x, k, m, k, nullptr, L, static_cast<uint8_t *>(out), static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "quantize launch");
+}
+
+cpq_status cpq_rms_norm(const float *x, const float *g, float *out, int64_t k, int64_t m, float eps, void *stream) {
+    if (!x || !out || k <= 0 || m < 0) return fail(CPQ_ERR_INVALID_ARG, "rms_norm arguments");
+    if (m == 0) return CPQ_SUCCESS;
+    if (m > 2147483647) return fail(CPQ_ERR_INVALID_ARG, "rms_norm: too many rows");
+    cudaError_t e = launch(rms_norm_kernel, dim3(unsigned(m)), dim3(256), 0, static_cast<cudaStream_t>(stream), x, g, out, k, eps);
+    return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "rms_norm launch");
+}
+
+cpq_status cpq_swiglu(const float *gate, const float *up, float *act, int64_t n, void *stream) {
+    if (!gate || !up || !act || n < 0) return fail(CPQ_ERR_INVALID_ARG, "swiglu arguments");
+    if (n == 0) return CPQ_SUCCESS;
+    cudaError_t e = launch(swiglu_kernel, dim3(unsigned(grid_1d(n, 256))), dim3(256), 0, static_cast<cudaStream_t>(stream), gate, up, act, n);
+    return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "swiglu launch");
+}
+
+cpq_status cpq_add_inplace(float *y, const float *x, int64_t n, void *stream) {
+    if (!y || !x || n < 0) return fail(CPQ_ERR_INVALID_ARG, "add arguments");
+    if (n == 0) return CPQ_SUCCESS;
+    cudaError_t e = launch(add_inplace_kernel, dim3(unsigned(grid_1d(n, 256))), dim3(256), 0, static_cast<cudaStream_t>(stream), y, x, n);
+    return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "add launch");
+}
+
+cpq_status cpq_argmax(const float *x, int64_t n, int64_t m, int32_t *out, void *stream) {
+    if (!x || !out || n <= 0 || m < 0 || n > 2147483647) return fail(CPQ_ERR_INVALID_ARG, "argmax arguments");
+    if (m == 0) return CPQ_SUCCESS;
+    cudaError_t e = launch(argmax_kernel, dim3(unsigned(m)), dim3(1024), 0, static_cast<cudaStream_t>(stream), x, n, out);
+    return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "argmax launch");
+}
+
+cpq_status cpq_synth_weights(int32_t type, void *dst, int64_t n_rows, int64_t n_blk, size_t row_stride, uint64_t seed,
+                             int64_t row0, int64_t blk0, void *stream) {
+    if (vec_dot_type(type) < 0) return fail(CPQ_ERR_UNSUPPORTED, "synth: type %s", type_name(type));
+    const int bb = int(type_bytes(type));
+    if (!dst || n_rows < 0 || n_blk < 0 || row0 < 0 || blk0 < 0) return fail(CPQ_ERR_INVALID_ARG, "synth arguments");
+    if (row_stride < size_t(n_blk) * size_t(bb) || row_stride % 2 || !aligned(dst, 2))
+        return fail(CPQ_ERR_INVALID_ARG, "synth: row stride %zu / alignment", row_stride);
+    if (n_rows == 0 || n_blk == 0) return CPQ_SUCCESS;
+    if (n_rows > 2147483647) return fail(CPQ_ERR_INVALID_ARG, "synth: too many rows");
+    cudaError_t e = launch(synth_kernel, dim3(unsigned(n_rows)), dim3(128), size_t(128) * bb, static_cast<cudaStream_t>(stream),
+                           type, static_cast<uint8_t *>(dst), n_blk, row_stride, bb, seed, row0, blk0);
+    return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "synth launch");
+}
+
+cpq_status cpq_device_status(int device, uint32_t *err_word, int clear) {
+    if (!err_word) return fail(CPQ_ERR_INVALID_ARG, "err_word is null");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(err_word, g_dev_error, sizeof(uint32_t));
+    if (e == cudaSuccess && clear) {
+        const uint32_t z = 0;
+        e = cudaMemcpyToSymbol(g_dev_error, &z, sizeof z);
+    }
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return cuda_fail(e, "device status");
+    return *err_word ? fail(CPQ_ERR_DEVICE, "device error word 0x%x", *err_word) : CPQ_SUCCESS;
+}
+
+// ---- NCCL -------------------------------------------------------------------
+
+cpq_status cpq_tp_unique_id(void *id128) {
+    if (!id128) return fail(CPQ_ERR_INVALID_ARG, "id buffer is null");
+    auto &n = nccl::api();
+    if (!n.ok) return fail(CPQ_ERR_NCCL, "libnccl.so.2 could not be loaded");
+    ncclUniqueId id;
+    const int r = n.GetUniqueId(&id);
+    if (r != ncclSuccess) return fail(CPQ_ERR_NCCL, "ncclGetUniqueId: %d", r);
+    std::memcpy(id128, &id, sizeof id);
+    return CPQ_SUCCESS;
+}
+
+cpq_status cpq_tp_comm_init(cpq_comm **comm, int nranks, int rank, const void *id128, int device, int timeout_ms) {
+    if (!comm || !id128 || nranks < 1 || rank < 0 || rank >= nranks || timeout_ms <= 0)
+        return fail(CPQ_ERR_INVALID_ARG, "comm_init arguments (nranks=%d rank=%d timeout=%d)", nranks, rank, timeout_ms);
+    *comm = nullptr;
+    auto &n = nccl::api();
+    if (!n.ok) return fail(CPQ_ERR_NCCL, "libnccl.so.2 could not be loaded");
+    ncclUniqueId id;
+    std::memcpy(&id, id128, sizeof id);
+    struct Init {
+        std::mutex mu;
+        bool done = false;
+        int rc = -1;
+        ncclComm_t c = nullptr;
+    };
+    auto st = std::make_shared<Init>();
+    std::thread th([st, nranks, rank, id, device, &n]() {
+        cudaSetDevice(device);
+        ncclComm_t c = nullptr;
+        const int r = n.CommInitRank(&c, nranks, id, rank);
+        std::lock_guard<std::mutex> lk(st->mu);
+        st->rc = r;
+        st->c = c;
+        st->done = true;
+    });
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
+    for (;;) {
+        {
+            std::lock_guard<std::mutex> lk(st->mu);
+            if (st->done) break;
+        }
+        if (std::chrono::steady_clock::now() > deadline) {
+            th.detach();  // a peer never joined; the blocked init thread is abandoned
+            return fail(CPQ_ERR_NCCL, "ncclCommInitRank did not finish within %d ms", timeout_ms);
+        }
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+    th.join();
+    if (st->rc != ncclSuccess) return fail(CPQ_ERR_NCCL, "ncclCommInitRank: %d", st->rc);
+    cpq_comm *c = new cpq_comm;
+    c->comm = st->c;
+    c->nranks = nranks;
+    c->rank = rank;
+    c->device = device;
+    c->timeout_ms = timeout_ms;
+    *comm = c;
+    return CPQ_SUCCESS;
+}
+
+cpq_status cpq_tp_allreduce_f32(cpq_comm *comm, float *buf, size_t n, void *stream) {
+    if (!comm || (!buf && n)) return fail(CPQ_ERR_INVALID_ARG, "allreduce arguments");
+    if (n == 0 || comm->nranks == 1) return CPQ_SUCCESS;
+    const int r = nccl::api().AllReduce(buf, buf, n, ncclFloat32, ncclSum, comm->comm, static_cast<cudaStream_t>(stream));
+    return r == ncclSuccess ? CPQ_SUCCESS : fail(CPQ_ERR_NCCL, "ncclAllReduce: %d", r);
+}
+
+cpq_status cpq_tp_comm_check(cpq_comm *comm) {
+    if (!comm) return fail(CPQ_ERR_INVALID_ARG, "comm is null");
+    int async = 0;
+    const int r = nccl::api().CommGetAsyncError(comm->comm, &async);
+    if (r != ncclSuccess) return fail(CPQ_ERR_NCCL, "ncclCommGetAsyncError: %d", r);
+    if (async != ncclSuccess && async != ncclInProgress) return fail(CPQ_ERR_NCCL, "communicator async error %d", async);
+    return CPQ_SUCCESS;
+}
+
+cpq_status cpq_tp_comm_destroy(cpq_comm *comm, int abort) {
+    if (!comm) return CPQ_SUCCESS;
+    auto &n = nccl::api();
+    const int r = abort ? n.CommAbort(comm->comm) : n.CommDestroy(comm->comm);
+    delete comm;
+    return r == ncclSuccess ? CPQ_SUCCESS : fail(CPQ_ERR_NCCL, "comm destroy/abort: %d", r);
+}
+
+}  // extern "C"

@@ -1,0 +1,194 @@
+// common.cuh — shared definitions for libcpq (sm_100a).
+//
+// Block formats (bytes per block from crates/codpiece-gguf/src/lib.rs:179-186):
+//   Q8_0: 32 elements, 34 B  = fp16 d, int8 qs[32]
+//   Q4_K: 256 elements, 144 B = fp16 d, fp16 dmin, u8 scales[12], u8 qs[128]
+//   Q6_K: 256 elements, 210 B = u8 ql[128], u8 qh[64], i8 scales[16], fp16 d
+//   Q8_K: 256 elements, 292 B = f32 d, i8 qs[256], i16 bsums[16]
+// Inside this library activations live in a structure-of-arrays form (all
+// quants of a row contiguous and 16-byte aligned, scales and 16-sums in
+// separate arrays) so kernels can use vector loads; cpq_quantize_act emits
+// the ggml array-of-structs bytes for callers that need them.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/cpq.h"
+
+namespace cpq {
+
+constexpr int kQK_K = 256;
+constexpr int kQK8_0 = 32;
+constexpr int kQ4K_Bytes = 144;
+constexpr int kQ6K_Bytes = 210;
+constexpr int kQ8_0_Bytes = 34;
+constexpr int kQ8K_Bytes = 292;
+
+// Device-side error word bits (read by cpq_device_status).
+enum : uint32_t {
+    kDevErrWaitTimeout = 1u << 0,  // a bounded mbarrier wait gave up
+    kDevErrBadLaunch = 1u << 1,    // a kernel saw arguments it cannot handle
+};
+
+// One word per device (a __device__ variable has one instance per device).
+__device__ uint32_t g_dev_error;
+
+// Upper bound for any spin on an mbarrier, in nanoseconds of %globaltimer.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+// ---- PTX helpers -----------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for phase `parity` of an mbarrier, giving up after kWaitLimitNs.
+// On give-up it records kDevErrWaitTimeout and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(&g_dev_error, kDevErrWaitTimeout);
+            return false;
+        }
+    }
+}
+
+// 1-D bulk copy global -> shared (TMA engine, no tensor map, no multicast).
+// dst, src 16-byte aligned; bytes a multiple of 16. Completion is signalled
+// as transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Same, with an L2 evict-first hint: weight bytes are streamed once per call.
+__device__ __forceinline__ void bulk_g2s_stream(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                                uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// Programmatic dependent launch: wait for the preceding grid's memory, and
+// let the next grid start its independent prologue early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// Read-only global loads that bypass L1 allocation-on-miss policy games.
+__device__ __forceinline__ int4 ldg_nc_v4(const void *p) {
+    int4 r;
+    asm volatile("ld.global.nc.v4.s32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// dot of 4 unsigned bytes (a) with 4 signed bytes (b), plus c.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// 16 bytes from shared memory at a 2-byte aligned address: five aligned
+// words and a funnel shift (shift 0 when the address is 4-byte aligned).
+__device__ __forceinline__ uint4 lds16_a2(const uint8_t *p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const uint32_t s = static_cast<uint32_t>(a & 3u) * 8u;
+    const uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3], w4 = w[4];
+    return make_uint4(__funnelshift_r(w0, w1, s), __funnelshift_r(w1, w2, s), __funnelshift_r(w2, w3, s),
+                      __funnelshift_r(w3, w4, s));
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t h16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(h16 & 0xffffu)));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ---- activation views ------------------------------------------------------
+
+// Quantized activations (structure of arrays) for M rows of K elements.
+//   qs:    int8 [M][K]            (row stride K bytes, 16-byte aligned)
+//   d:     f32  [M][K/blk]        (Q8_K: 1/iscale; Q8_0: the fp16 d widened)
+//   bsums: i16  [M][K/16]         (Q8_K only)
+struct ActQ {
+    const int8_t *qs;
+    const float *d;
+    const int16_t *bsums;
+};
+
+// Workspace carve-up for quantized activations.
+struct ActLayout {
+    size_t qs_off, d_off, bs_off, bytes;
+};
+
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+inline ActLayout act_layout(int vec_type, int64_t k, int64_t m) {
+    ActLayout l;
+    const int64_t blk = vec_type == CPQ_TYPE_Q8_K ? kQK_K : kQK8_0;
+    l.qs_off = 0;
+    l.d_off = align_up(size_t(m) * size_t(k), 256);
+    l.bs_off = align_up(l.d_off + size_t(m) * size_t(k / blk) * 4, 256);
+    l.bytes = align_up(l.bs_off + (vec_type == CPQ_TYPE_Q8_K ? size_t(m) * size_t(k / 16) * 2 : 0), 256);
+    return l;
+}
+
+}  // namespace cpq

@@ -1,0 +1,102 @@
+// elementwise.cuh — the small ops around the projections of a decode layer:
+// rms norm (qwen35.rs:2534-2537, ggml_rms_norm + ggml_mul), SwiGLU
+// (qwen35.rs:2781, ggml_silu + ggml_mul), residual add (qwen35.rs:2777, 2783)
+// and the greedy argmax after the LM head (qwen35.rs:2800-2818).
+#pragma once
+
+#include "common.cuh"
+
+namespace cpq {
+
+// ggml-cpu rms_norm: sum of x*x (each product rounded to fp32, summed in
+// double), mean = sum/k as fp32, scale = 1/sqrt(mean + eps), y = x*scale;
+// then the weight multiply of rms(). One CTA per row.
+__global__ void __launch_bounds__(256) rms_norm_kernel(const float *__restrict__ x, const float *__restrict__ g,
+                                                       float *__restrict__ out, int64_t k, float eps) {
+    pdl_wait();
+    pdl_launch_dependents();
+    __shared__ double part[8];
+    const int64_t row = blockIdx.x;
+    const float *xr = x + row * k;
+    double s = 0.0;
+    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+        const float v = xr[i];
+        s += double(__fmul_rn(v, v));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    double tot = 0.0;
+    for (int w = 0; w < int(blockDim.x >> 5); w++) tot += part[w];
+    const float mean = float(tot / double(k));
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    float *orow = out + row * k;
+    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+        const float v = __fmul_rn(xr[i], scale);
+        orow[i] = g ? __fmul_rn(v, g[i]) : v;
+    }
+}
+
+// ggml silu(x) = x / (1 + exp(-x)); act = silu(gate) * up.
+__global__ void swiglu_kernel(const float *__restrict__ gate, const float *__restrict__ up, float *__restrict__ act,
+                              int64_t n) {
+    pdl_wait();
+    pdl_launch_dependents();
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const float gv = gate[i];
+        const float s = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
+        act[i] = __fmul_rn(s, up[i]);
+    }
+}
+
+__global__ void add_inplace_kernel(float *__restrict__ y, const float *__restrict__ x, int64_t n) {
+    pdl_wait();
+    pdl_launch_dependents();
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+        y[i] = __fadd_rn(y[i], x[i]);
+}
+
+// First index of the maximum of each row (NaN-free input assumed).
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ x, int64_t n,
+                                                     int32_t *__restrict__ out) {
+    pdl_wait();
+    pdl_launch_dependents();
+    __shared__ float sv[32];
+    __shared__ int32_t si[32];
+    const float *xr = x + int64_t(blockIdx.x) * n;
+    float best = -INFINITY;
+    int32_t bi = 0x7fffffff;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = xr[i];
+        if (v > best) {
+            best = v;
+            bi = int32_t(i);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        sv[w] = best;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int q = 1; q < int(blockDim.x >> 5); q++)
+            if (sv[q] > best || (sv[q] == best && si[q] < bi)) {
+                best = sv[q];
+                bi = si[q];
+            }
+        out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
+}  // namespace cpq

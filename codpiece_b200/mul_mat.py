@@ -1,0 +1,213 @@
+"""Host-side mirror of ggml's mul_mat operator surface over libcpq.
+
+ggml's contract (crates/codpiece-ggml-sys/tests/smoke.rs:29-54): W has
+ne = [K, N], X has ne = [K, M] (F32), and mul_mat(W, X) has ne = [N, M] with
+Y[m, n] = dot(W row n, X row m). In torch terms X is a [M, K] float32 tensor
+and Y a [M, N] float32 tensor; W is a :class:`QTensor` holding ggml's packed
+row bytes on the device.
+
+Every call goes through the C ABI of libcpq.so (include/cpq.h). There is no
+CPU or PyTorch fallback: a missing library or an unsupported shape raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import CpqTensor, check, lib
+
+TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_K = (
+    _lib.TYPE_F32, _lib.TYPE_Q8_0, _lib.TYPE_Q4_K, _lib.TYPE_Q6_K, _lib.TYPE_Q8_K)
+
+# (elements per block, bytes per block): crates/codpiece-gguf/src/lib.rs:179-186
+BLOCK = {TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144), TYPE_Q6_K: (256, 210), TYPE_Q8_K: (256, 292)}
+TYPE_NAMES = {TYPE_Q8_0: "Q8_0", TYPE_Q4_K: "Q4_K", TYPE_Q6_K: "Q6_K", TYPE_Q8_K: "Q8_K", TYPE_F32: "F32"}
+VEC_DOT_TYPE = {TYPE_Q4_K: TYPE_Q8_K, TYPE_Q6_K: TYPE_Q8_K, TYPE_Q8_0: TYPE_Q8_0}
+
+DEFAULT_WORKSPACE = 64 << 20
+
+
+def row_bytes(qtype: int, k: int) -> int:
+    blk, size = BLOCK[qtype]
+    if k % blk:
+        raise ValueError(f"K={k} is not a multiple of the {TYPE_NAMES[qtype]} block ({blk})")
+    return k // blk * size
+
+
+@dataclass
+class QTensor:
+    """A quantized weight in ggml layout on a CUDA device.
+
+    ``data`` is a uint8 CUDA tensor of N rows x row_stride bytes; ``k``/``n``
+    are ggml's ne[0]/ne[1].
+    """
+
+    qtype: int
+    k: int
+    n: int
+    data: torch.Tensor
+    row_stride: int = 0
+
+    def __post_init__(self):
+        if self.row_stride == 0:
+            self.row_stride = row_bytes(self.qtype, self.k)
+        if self.data.dtype != torch.uint8 or not self.data.is_cuda:
+            raise TypeError("QTensor.data must be a uint8 CUDA tensor")
+        if self.data.numel() < self.n * self.row_stride:
+            raise ValueError("QTensor.data is smaller than n * row_stride")
+
+    @classmethod
+    def from_numpy(cls, qtype: int, k: int, n: int, blocks: np.ndarray, device="cuda") -> "QTensor":
+        """Upload packed ggml rows (uint8 [n, row_bytes]) to the device."""
+        rb = row_bytes(qtype, k)
+        arr = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(n, rb)
+        return cls(qtype, k, n, torch.from_numpy(arr).to(device).reshape(-1), rb)
+
+    @classmethod
+    def empty(cls, qtype: int, k: int, n: int, device="cuda") -> "QTensor":
+        rb = row_bytes(qtype, k)
+        return cls(qtype, k, n, torch.empty(n * rb, dtype=torch.uint8, device=device), rb)
+
+    @property
+    def nbytes(self) -> int:
+        return self.n * row_bytes(self.qtype, self.k)
+
+    def desc(self) -> CpqTensor:
+        d = CpqTensor()
+        d.type = self.qtype
+        d.ne[:] = [self.k, self.n, 1, 1]
+        bs = BLOCK[self.qtype][1]
+        d.nb[:] = [bs, self.row_stride, self.row_stride * self.n, self.row_stride * self.n]
+        d.data = self.data.data_ptr()
+        return d
+
+
+def f32_desc(t: torch.Tensor) -> CpqTensor:
+    """ggml descriptor of a [M, K] float32 tensor (ne = [K, M])."""
+    if t.dtype != torch.float32 or t.dim() != 2 or t.stride(1) != 1:
+        raise TypeError("expected a 2-D float32 tensor with contiguous rows")
+    d = CpqTensor()
+    d.type = TYPE_F32
+    m, k = t.shape
+    d.ne[:] = [k, m, 1, 1]
+    d.nb[:] = [4, t.stride(0) * 4, t.stride(0) * 4 * m, t.stride(0) * 4 * m]
+    d.data = t.data_ptr()
+    return d
+
+
+def _stream(stream) -> C.c_void_p:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+_ws_bytes: dict[int, int] = {}
+
+
+def init(device: int | None = None, workspace_bytes: int = DEFAULT_WORKSPACE) -> None:
+    """Allocate (or grow) libcpq's per-device workspace. Call before graph capture."""
+    dev = torch.cuda.current_device() if device is None else int(device)
+    if _ws_bytes.get(dev, 0) >= workspace_bytes:
+        return
+    check(lib().cpq_init(dev, workspace_bytes), "cpq_init")
+    _ws_bytes[dev] = workspace_bytes
+
+
+def _ensure_workspace(w: QTensor, x: torch.Tensor) -> None:
+    dev = x.device.index if x.device.index is not None else torch.cuda.current_device()
+    need = lib().cpq_mul_mat_workspace_size(C.byref(w.desc()), C.byref(f32_desc(x)))
+    if _ws_bytes.get(dev, 0) < need:
+        init(dev, max(need, DEFAULT_WORKSPACE))
+
+
+def mul_mat(w: QTensor, x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """ggml_mul_mat(W, X) executed on the GPU: returns Y [M, N] float32."""
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    if out is None:
+        out = torch.empty(x.shape[0], w.n, dtype=torch.float32, device=x.device)
+    _ensure_workspace(w, x)
+    wd, xd, yd = w.desc(), f32_desc(x), f32_desc(out)
+    check(lib().cpq_mul_mat(C.byref(wd), C.byref(xd), C.byref(yd), _stream(stream)), "cpq_mul_mat")
+    return out
+
+
+def mul_mat_multi(ws: list[QTensor], x: torch.Tensor, outs: list[torch.Tensor] | None = None,
+                  stream=None) -> list[torch.Tensor]:
+    """Several weights sharing one input (q/k/v, gate/up): one quantization, one launch."""
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    if outs is None:
+        outs = [torch.empty(x.shape[0], w.n, dtype=torch.float32, device=x.device) for w in ws]
+    _ensure_workspace(ws[0], x)
+    wds = [w.desc() for w in ws]
+    yds = [f32_desc(o) for o in outs]
+    xd = f32_desc(x)
+    n = len(ws)
+    warr = (C.POINTER(CpqTensor) * n)(*[C.pointer(d) for d in wds])
+    yarr = (C.POINTER(CpqTensor) * n)(*[C.pointer(d) for d in yds])
+    check(lib().cpq_mul_mat_multi(warr, yarr, n, C.byref(xd), _stream(stream)), "cpq_mul_mat_multi")
+    return outs
+
+
+def quantize_act(wtype: int, x: torch.Tensor, stream=None) -> torch.Tensor:
+    """ggml-cpu's re-quantization of X rows to W's vec_dot_type, as raw ggml block bytes."""
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    x = x.contiguous()
+    m, k = x.shape
+    vt = VEC_DOT_TYPE[wtype]
+    out = torch.empty(m * row_bytes(vt, k), dtype=torch.uint8, device=x.device)
+    check(lib().cpq_quantize_act(wtype, C.c_void_p(x.data_ptr()), C.c_void_p(out.data_ptr()), k, m, _stream(stream)),
+          "cpq_quantize_act")
+    return out.view(m, -1)
+
+
+def rms_norm(x: torch.Tensor, g: torch.Tensor | None = None, eps: float = 1e-6, out=None, stream=None):
+    m, k = x.shape
+    out = torch.empty_like(x) if out is None else out
+    check(lib().cpq_rms_norm(C.c_void_p(x.data_ptr()), C.c_void_p(g.data_ptr() if g is not None else 0),
+                             C.c_void_p(out.data_ptr()), k, m, eps, _stream(stream)), "cpq_rms_norm")
+    return out
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor, out=None, stream=None):
+    out = torch.empty_like(gate) if out is None else out
+    check(lib().cpq_swiglu(C.c_void_p(gate.data_ptr()), C.c_void_p(up.data_ptr()), C.c_void_p(out.data_ptr()),
+                           gate.numel(), _stream(stream)), "cpq_swiglu")
+    return out
+
+
+def add_(y: torch.Tensor, x: torch.Tensor, stream=None):
+    check(lib().cpq_add_inplace(C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()), y.numel(), _stream(stream)),
+          "cpq_add_inplace")
+    return y
+
+
+def argmax(x: torch.Tensor, out=None, stream=None) -> torch.Tensor:
+    m, n = x.shape
+    out = torch.empty(m, dtype=torch.int32, device=x.device) if out is None else out
+    check(lib().cpq_argmax(C.c_void_p(x.data_ptr()), n, m, C.c_void_p(out.data_ptr()), _stream(stream)), "cpq_argmax")
+    return out
+
+
+def synth_weights(qtype: int, k: int, n: int, seed: int, row0: int = 0, blk0: int = 0, k_blocks: int | None = None,
+                  device="cuda", stream=None) -> QTensor:
+    """Seeded synthetic weight rows [row0, row0+n) x blocks [blk0, blk0+k_blocks) generated on the device."""
+    blk, _ = BLOCK[qtype]
+    nblk = k // blk if k_blocks is None else k_blocks
+    w = QTensor.empty(qtype, nblk * blk, n, device=device)
+    check(lib().cpq_synth_weights(qtype, C.c_void_p(w.data.data_ptr()), n, nblk, w.row_stride, seed, row0, blk0,
+                                  _stream(stream)), "cpq_synth_weights")
+    return w
+
+
+def device_status(device: int = 0, clear: bool = True) -> int:
+    word = C.c_uint32(0)
+    rc = lib().cpq_device_status(device, C.byref(word), 1 if clear else 0)
+    if rc not in (0, 7):
+        check(rc, "cpq_device_status")
+    return word.value

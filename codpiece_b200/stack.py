@@ -1,0 +1,207 @@
+"""The 27B-shaped quantized decoder stack, tensor-parallel over N GPUs.
+
+This is the benchmark's multi-GPU workload: n_layer layers of random-init
+Q4_K projections (hidden 5120, q 6144, k/v 1024, FFN 17408) and a Q6_K LM
+head over vocab 151936, run as decode (M = 1) or verify (M = 2..16) steps.
+Each layer follows codpiece's qwen35 trunk (crates/codpiece-model/src/
+qwen35.rs:2554-2786) with the attention core left out:
+
+    xn = rms_norm(h)                             (2534-2537)
+    q, k, v = W_q xn, W_k xn, W_v xn             (3029, 3047, 3051)
+    h = h + allreduce(W_o q)                     (3197; q stands in for the attention output)
+    xn = rms_norm(h)
+    g, u = W_gate xn, W_up xn                    (2779-2780)
+    h = h + allreduce(W_down (silu(g) * u))      (2781-2783)
+    token = argmax(W_head rms_norm(h))           (2797-2818)
+
+Tensor parallelism follows the reference's split rules (cpq_tp_split_state):
+q/k/v/gate/up column-parallel (each rank owns output rows), attn_output and
+ffn_down row-parallel (each rank owns a K range of quant blocks; its fp32
+partials are summed by an NCCL allreduce), the LM head mirrored. One process
+per GPU; every op is a libcpq call, and a whole step is captured in one CUDA
+graph per rank.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from . import mul_mat as mm
+from . import tp
+from ._lib import check, lib
+
+KIND_IDS = {"q": 0, "k": 1, "v": 2, "o": 3, "gate": 4, "up": 5, "down": 6, "head": 7}
+
+
+def tensor_seed(seed: int, layer: int, kind: str) -> int:
+    return (seed * 1_000_003 + layer * 16 + KIND_IDS[kind]) & 0xFFFFFFFFFFFFFFFF
+
+
+@dataclass
+class LayerWeights:
+    q: mm.QTensor | None
+    k: mm.QTensor | None
+    v: mm.QTensor | None
+    o: mm.QTensor | None
+    gate: mm.QTensor | None
+    up: mm.QTensor | None
+    down: mm.QTensor | None
+
+
+class Comm:
+    """NCCL communicator of one rank (cpq_tp_comm_* in include/cpq.h)."""
+
+    def __init__(self, nranks: int, rank: int, uid: bytes, device: int, timeout_ms: int = 60000):
+        self.handle = C.c_void_p()
+        buf = C.create_string_buffer(uid, 128)
+        check(lib().cpq_tp_comm_init(C.byref(self.handle), nranks, rank, buf, device, timeout_ms), "cpq_tp_comm_init")
+        self.nranks = nranks
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        check(lib().cpq_tp_unique_id(buf), "cpq_tp_unique_id")
+        return buf.raw
+
+    def allreduce_(self, t: torch.Tensor, stream=None) -> None:
+        s = (stream or torch.cuda.current_stream()).cuda_stream
+        check(lib().cpq_tp_allreduce_f32(self.handle, C.c_void_p(t.data_ptr()), t.numel(), C.c_void_p(s)),
+              "cpq_tp_allreduce_f32")
+
+    def check(self) -> None:
+        check(lib().cpq_tp_comm_check(self.handle), "cpq_tp_comm_check")
+
+    def destroy(self, abort: bool = False) -> None:
+        if self.handle:
+            lib().cpq_tp_comm_destroy(self.handle, 1 if abort else 0)
+            self.handle = C.c_void_p()
+
+
+class Stack:
+    """This rank's shard of the stack plus its activation buffers."""
+
+    def __init__(self, hp: tp.Hparams, n_layer: int, rank: int = 0, world: int = 1, comm: Comm | None = None,
+                 m: int = 1, seed: int = 0, head: bool = True, device: int | None = None, eps: float = 1e-6):
+        self.hp, self.n_layer, self.rank, self.world, self.comm, self.m = hp, n_layer, rank, world, comm, m
+        self.eps = eps
+        self.dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        e = hp.n_embd
+        nb_e = e // 256
+        self.layers: list[LayerWeights] = []
+        self.shards: list[tp.LayerShards] = []
+        for il in range(n_layer):
+            sh = tp.layer_shards(hp, il, world)
+            self.shards.append(sh)
+            (q0, q1), (k0, k1), (v0, v1) = sh.q[rank], sh.k[rank], sh.v[rank]
+            (o0, o1), (f0, f1), (d0, d1) = sh.o[rank], sh.gate[rank], sh.down[rank]
+
+            def rows(kind, r0, r1, k_elems=e):
+                if r1 <= r0:
+                    return None
+                return mm.synth_weights(mm.TYPE_Q4_K, k_elems, r1 - r0, tensor_seed(seed, il, kind), row0=r0,
+                                        device=self.dev)
+
+            def kslice(kind, n_rows, c0, c1):
+                if c1 <= c0:
+                    return None
+                return mm.synth_weights(mm.TYPE_Q4_K, c1 - c0, n_rows, tensor_seed(seed, il, kind), row0=0,
+                                        blk0=c0 // 256, device=self.dev)
+
+            self.layers.append(LayerWeights(
+                q=rows("q", q0, q1), k=rows("k", k0, k1), v=rows("v", v0, v1), o=kslice("o", e, o0, o1),
+                gate=rows("gate", f0, f1), up=rows("up", f0, f1), down=kslice("down", e, d0, d1)))
+        self.head = (mm.synth_weights(mm.TYPE_Q6_K, e, hp.n_vocab, tensor_seed(seed, 0, "head"), device=self.dev)
+                     if head else None)
+        del nb_e
+        f = lambda n: torch.zeros(m, n, dtype=torch.float32, device=self.dev)  # noqa: E731
+        qmax = max((s.q[rank][1] - s.q[rank][0]) for s in self.shards) or 1
+        kmax = max((s.k[rank][1] - s.k[rank][0]) for s in self.shards) or 1
+        fmax = max((s.gate[rank][1] - s.gate[rank][0]) for s in self.shards) or 1
+        self.h, self.xn = f(e), f(e)
+        self.qb, self.kb, self.vb = f(qmax), f(kmax), f(kmax)
+        self.part = f(e)
+        self.gb, self.ub, self.act = f(fmax), f(fmax), f(fmax)
+        self.logits = f(hp.n_vocab) if head else None
+        self.tok = torch.zeros(m, dtype=torch.int32, device=self.dev)
+        mm.init(self.dev.index, 64 << 20)
+        self.graph: torch.cuda.CUDAGraph | None = None
+
+    # -- bytes -------------------------------------------------------------
+    def weight_bytes(self) -> int:
+        n = 0
+        for lw in self.layers:
+            for w in (lw.q, lw.k, lw.v, lw.o, lw.gate, lw.up, lw.down):
+                n += w.nbytes if w is not None else 0
+        return n + (self.head.nbytes if self.head is not None else 0)
+
+    def launches_per_step(self) -> int:
+        """libcpq kernels one step launches (NCCL's own kernels not counted)."""
+        n = 0
+        for lw in self.layers:
+            n += 2  # rms norms
+            if lw.q is not None or lw.k is not None or lw.v is not None:
+                n += 2  # quantize + fused q/k/v gemv
+            n += 2 if lw.o is not None else 0
+            n += 1  # residual add
+            n += 2 + 1 + 2 + 1  # gate/up (quantize + gemv), swiglu, down (quantize + gemv), add
+        if self.head is not None:
+            n += 1 + 2 + 1
+        return n
+
+    # -- one step ----------------------------------------------------------
+    def _sl(self, buf: torch.Tensor, n: int) -> torch.Tensor:
+        # a contiguous [m, n] view at the front of a flat buffer
+        return buf.view(-1)[: self.m * n].view(self.m, n)
+
+    def step_body(self) -> None:
+        """Enqueue one decode/verify step on the current stream (h is updated in place)."""
+        for il, lw in enumerate(self.layers):
+            mm.rms_norm(self.h, None, self.eps, out=self.xn)
+            ws, outs = [], []
+            for w, b in ((lw.q, self.qb), (lw.k, self.kb), (lw.v, self.vb)):
+                if w is not None:
+                    ws.append(w)
+                    outs.append(self._sl(b, w.n))
+            if ws:
+                mm.mul_mat_multi(ws, self.xn, outs)
+            if lw.o is not None:
+                mm.mul_mat(lw.o, self._sl(self.qb, lw.o.k), out=self.part)
+            else:
+                self.part.zero_()
+            if self.world > 1:
+                self.comm.allreduce_(self.part)
+            mm.add_(self.h, self.part)
+            mm.rms_norm(self.h, None, self.eps, out=self.xn)
+            nf = lw.gate.n
+            g, u, a = self._sl(self.gb, nf), self._sl(self.ub, nf), self._sl(self.act, nf)
+            mm.mul_mat_multi([lw.gate, lw.up], self.xn, [g, u])
+            mm.swiglu(g, u, out=a)
+            mm.mul_mat(lw.down, a, out=self.part)
+            if self.world > 1:
+                self.comm.allreduce_(self.part)
+            mm.add_(self.h, self.part)
+        if self.head is not None:
+            mm.rms_norm(self.h, None, self.eps, out=self.xn)
+            mm.mul_mat(self.head, self.xn, out=self.logits)
+            mm.argmax(self.logits, out=self.tok)
+
+    def capture(self) -> None:
+        """Capture step_body() into a CUDA graph (run one eager step first to warm up)."""
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self.step_body()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize(self.dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step_body()
+        self.graph = g
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+    def release(self) -> None:
+        self.graph = None

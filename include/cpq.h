@@ -1,0 +1,201 @@
+/*
+ * cpq.h — C ABI of codpiece-b200's quantized mul_mat (libcpq.so).
+ *
+ * Drop-in target: the ggml_mul_mat node that codpiece's graph builder issues
+ * for every projection (crates/codpiece-model/src/qwen35.rs:2575-2583, 2758,
+ * 2779-2782, 2797, 3029, 3047, 3051, 3197; mtp_graph.rs:184-230; dflash.rs:
+ * 449-847). codpiece reaches ggml through bindgen over
+ * crates/codpiece-ggml-sys/wrapper.h:1-9 (build.rs:108-127); this header is
+ * written to be consumed the same way (plain C, no CUDA or torch types: the
+ * stream is a void*).
+ *
+ * Conventions follow ggml (crates/codpiece-ggml-sys/tests/smoke.rs:29-54):
+ *   W: ne = [K, N], type Q4_K / Q6_K / Q8_0, rows of K contiguous blocks
+ *   X: ne = [K, M], F32
+ *   Y: ne = [N, M], F32, Y[m*N + n] = dot(W row n, X row m)
+ * with X re-quantized on the device to W's vec_dot_type (Q8_K for Q4_K/Q6_K,
+ * Q8_0 for Q8_0) exactly as ggml-cpu does before its integer block dots.
+ *
+ * All pointers in cpq_tensor.data are device pointers owned by the caller.
+ * Every call is asynchronous on the given stream. No call aborts: failures
+ * return a cpq_status and cpq_last_error() describes the last one on the
+ * calling thread.
+ */
+#ifndef CPQ_H
+#define CPQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CPQ_ABI_VERSION 1
+
+/* ggml_type ids as serialized in GGUF (crates/codpiece-gguf/src/lib.rs:170-205). */
+typedef enum {
+    CPQ_TYPE_F32 = 0,
+    CPQ_TYPE_F16 = 1,
+    CPQ_TYPE_Q8_0 = 8,
+    CPQ_TYPE_Q4_K = 12,
+    CPQ_TYPE_Q6_K = 14,
+    CPQ_TYPE_Q8_K = 15,
+} cpq_type;
+
+/* Status codes. 0 matches GGML_STATUS_SUCCESS; a non-zero status is what the
+ * caller maps to its own error (codpiece: qwen35.rs:3617-3619 maps a
+ * non-SUCCESS compute status to ModelError). */
+typedef enum {
+    CPQ_SUCCESS = 0,
+    CPQ_ERR_INVALID_ARG = 1,     /* null pointer, shape mismatch, bad size */
+    CPQ_ERR_UNSUPPORTED = 2,     /* type/layout outside the fast path */
+    CPQ_ERR_NOT_INITIALIZED = 3, /* no workspace on the current device */
+    CPQ_ERR_WORKSPACE = 4,       /* workspace too small for this call */
+    CPQ_ERR_CUDA = 5,            /* a CUDA runtime call failed */
+    CPQ_ERR_NCCL = 6,            /* NCCL missing or a collective failed */
+    CPQ_ERR_DEVICE = 7,          /* a kernel reported a device-side error */
+} cpq_status;
+
+/* Tensor descriptor: the subset of ggml_tensor (ggml.h: type, ne[4], nb[4],
+ * data) the operator reads. ne[0] is the contiguous dimension; nb are byte
+ * strides. */
+typedef struct cpq_tensor {
+    int32_t type;
+    int64_t ne[4];
+    size_t nb[4];
+    void *data;
+} cpq_tensor;
+
+/* ---- library / device set-up ------------------------------------------- */
+
+/* Allocates the per-device workspace the hot calls use (activation blocks and
+ * split partials) so that cpq_mul_mat never allocates. Replaces the pool that
+ * ggml-cuda's backend context owns for its mul_mat scratch. Calling it again
+ * with a larger size grows the workspace (not during stream capture). */
+cpq_status cpq_init(int device, size_t workspace_bytes);
+/* Frees the workspace of one device. */
+cpq_status cpq_release(int device);
+
+/* Workspace bytes cpq_mul_mat/cpq_mul_mat_ws need for this W/X pair. */
+size_t cpq_mul_mat_workspace_size(const cpq_tensor *w, const cpq_tensor *x);
+
+/* ---- the operator -------------------------------------------------------- */
+
+/* Y = W x quantize(X): the execution of ggml_mul_mat(ctx, W, X)
+ * (ggml.h ggml_mul_mat; call sites listed at the top of this file) for
+ * W in {Q4_K, Q6_K, Q8_0}, X/Y F32, any M >= 1, ne[2] = ne[3] = 1.
+ * Other types or layouts return CPQ_ERR_UNSUPPORTED without launching
+ * anything. Uses the workspace from cpq_init on the current device. */
+cpq_status cpq_mul_mat(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *y, void *stream);
+
+/* Same, with a caller-provided device workspace (e.g. from ggml-cuda's pool). */
+cpq_status cpq_mul_mat_ws(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *y, void *workspace,
+                          size_t workspace_bytes, void *stream);
+
+/* Several weights that share one input X (q/k/v at qwen35.rs:3029-3051,
+ * gate/up at qwen35.rs:2779-2780): X is quantized once and all n_w products
+ * run in one launch. Every w[i] must have the same type and K. */
+cpq_status cpq_mul_mat_multi(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
+                             void *stream);
+
+/* Activation re-quantization as ggml-cpu's from_float for the vec_dot_type of
+ * wtype (Q8_K for Q4_K/Q6_K, Q8_0 for Q8_0): m rows of k floats (row stride k)
+ * into m*k/blck ggml blocks (block_q8_K 292 B, block_q8_0 34 B) at out. */
+cpq_status cpq_quantize_act(int32_t wtype, const float *x, void *out, int64_t k, int64_t m, void *stream);
+
+/* Fused decode prologue: out = rmsnorm(x) * g (g may be NULL for unit weight),
+ * as codpiece's rms() (qwen35.rs:2534-2537: ggml_rms_norm then ggml_mul).
+ * m rows of k floats. */
+cpq_status cpq_rms_norm(const float *x, const float *g, float *out, int64_t k, int64_t m, float eps,
+                        void *stream);
+
+/* act = silu(gate) * up, elementwise over n floats (qwen35.rs:2781). */
+cpq_status cpq_swiglu(const float *gate, const float *up, float *act, int64_t n, void *stream);
+
+/* y += x, elementwise over n floats (the residual adds, qwen35.rs:2777, 2783). */
+cpq_status cpq_add_inplace(float *y, const float *x, int64_t n, void *stream);
+
+/* Per-row argmax of m rows of n floats (first index on ties), the in-graph
+ * greedy pick after the LM head (qwen35.rs:2800-2818). */
+cpq_status cpq_argmax(const float *x, int64_t n, int64_t m, int32_t *out, void *stream);
+
+/* ---- tensor parallel ------------------------------------------------------ */
+
+/* Split axis values (crates/codpiece-model/src/split.rs:17-31). */
+typedef enum {
+    CPQ_SPLIT_AXIS_0 = 0,    /* split ne[0] (K): row-parallel, ends in an allreduce */
+    CPQ_SPLIT_AXIS_1 = 1,    /* split ne[1] (N): column-parallel */
+    CPQ_SPLIT_AXIS_2 = 2,
+    CPQ_SPLIT_MIRRORED = 3,
+    CPQ_SPLIT_PARTIAL = 4,
+} cpq_split_axis;
+
+/* Model hyper-parameters the split rules read (qwen35.rs:45-148 Hparams).
+ * q_has_gate = 1 for the real qwen35 attn_q (Q and gate interleaved, 2x the
+ * q width); 0 for a plain q projection of n_head*head_k rows. */
+typedef struct cpq_hparams {
+    int64_t n_layer, n_embd, n_head, n_head_kv, head_k, head_v, n_ff;
+    int64_t n_k_heads, n_v_heads, d_state, d_inner, full_attn_interval, n_vocab;
+    int32_t q_has_gate;
+    int32_t split_output; /* CODPIECE_SPLIT_OUTPUT: column-split the LM head */
+} cpq_hparams;
+
+/* The per-device split of one tensor: the C-facing SplitState
+ * (split.rs:285-294) in the shape of ggml's meta-backend callback result
+ * (meta.rs:50-121): ne[segment * n_devices + device], nr[segment]. */
+typedef struct cpq_split_state {
+    int32_t axis;
+    uint32_t n_segments;
+    int64_t ne[256];
+    uint32_t nr[16];
+} cpq_split_state;
+
+/* split.rs:298-333 split_state(): classify the tensor by name, honour its
+ * segments, granularity (blck = block size of the axis-0 reference tensor's
+ * type) and per-layer rotation. Never fails: unknown names, bad arguments and
+ * too many devices fall back to MIRRORED, like meta.rs:47-64. */
+cpq_split_state cpq_tp_split_state(const char *name, const cpq_hparams *hp, int64_t extent, int64_t blck,
+                                   int n_devices);
+
+/* NCCL communicator for one rank of a tensor-parallel group (one process per
+ * GPU). NCCL is loaded on first use (libnccl.so.2). The 128-byte unique id is
+ * produced by rank 0 and shared by the caller (e.g. a torch.distributed
+ * store). timeout_ms bounds every blocking wait in this API. */
+typedef struct cpq_comm cpq_comm;
+cpq_status cpq_tp_unique_id(void *id128);
+cpq_status cpq_tp_comm_init(cpq_comm **comm, int nranks, int rank, const void *id128, int device,
+                            int timeout_ms);
+/* In-place sum of n floats across the group (the allreduce ggml's meta
+ * backend inserts after every row-parallel product, docs/OPTIMIZATION-IDEAS.md:
+ * 21-29). Enqueued on stream; asynchronous. */
+cpq_status cpq_tp_allreduce_f32(cpq_comm *comm, float *buf, size_t n, void *stream);
+/* Polls the communicator for an asynchronous error (ncclCommGetAsyncError). */
+cpq_status cpq_tp_comm_check(cpq_comm *comm);
+/* Destroys (or, with abort != 0, aborts) the communicator. */
+cpq_status cpq_tp_comm_destroy(cpq_comm *comm, int abort);
+
+/* ---- synthetic weights ----------------------------------------------------- */
+
+/* Fills rows [row0, row0+n_rows) x blocks [blk0, blk0+n_blk) of a tensor of
+ * the given type with seeded synthetic blocks (the value distributions of the
+ * benchmark configs: fp16 scales |N(0,sigma)|, uniform quants/scales), as a
+ * pure function of (seed, global row, global block, byte). dst holds n_rows
+ * rows of row_stride bytes. Used for random-init weights of the 27B-shaped
+ * stack; a shard generated this way equals the same slice of the whole. */
+cpq_status cpq_synth_weights(int32_t type, void *dst, int64_t n_rows, int64_t n_blk, size_t row_stride,
+                             uint64_t seed, int64_t row0, int64_t blk0, void *stream);
+
+/* ---- diagnostics ------------------------------------------------------------ */
+
+/* Reads (and with clear != 0 resets) the device-side error word that kernels
+ * set when a bounded wait gives up. Synchronizes the device. */
+cpq_status cpq_device_status(int device, uint32_t *err_word, int clear);
+const char *cpq_last_error(void);
+const char *cpq_status_string(cpq_status s);
+int cpq_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

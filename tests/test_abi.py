@@ -1,0 +1,106 @@
+"""The C-ABI library loads and exports every entry point include/cpq.h declares.
+
+CPU only: no compute call is made; host-side validation paths that return
+before touching a device are exercised.
+"""
+import ctypes as C
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "cpq.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(cpq_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def L():
+    from codpiece_b200 import _lib, build
+    build.build()
+    return _lib.lib()
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for must in ("cpq_mul_mat", "cpq_quantize_act", "cpq_tp_allreduce_f32", "cpq_tp_split_state", "cpq_last_error",
+                 "cpq_init"):
+        assert must in names
+
+
+def test_every_declared_symbol_is_exported(L):
+    from codpiece_b200 import _lib
+    lib_path = _lib.LIB_PATH
+    out = subprocess.run(["nm", "-D", "--defined-only", str(lib_path)], capture_output=True, text=True, check=True)
+    exported = set(re.findall(r"\b(cpq_[a-z0-9_]+)\b", out.stdout))
+    missing = [n for n in declared_functions() if n not in exported]
+    assert not missing, missing
+    assert sorted(_lib.EXPORTED) == declared_functions()
+    for n in declared_functions():
+        assert hasattr(L, n)
+
+
+def test_library_is_sm100a_only_and_links_no_nccl(L):
+    from codpiece_b200 import _lib
+    out = subprocess.run(["readelf", "-d", str(_lib.LIB_PATH)], capture_output=True, text=True, check=True).stdout
+    assert "libnccl" not in out  # NCCL is dlopen'ed on first use
+    assert "libtorch" not in out
+    src = (ROOT / "codpiece_b200" / "build.py").read_text()
+    assert "arch=compute_100a,code=sm_100a" in src
+
+
+def test_version_and_status_strings(L):
+    assert L.cpq_abi_version() == 1
+    assert L.cpq_status_string(0) == b"success"
+    assert L.cpq_status_string(2) == b"unsupported"
+
+
+def test_validation_rejects_before_any_device_work(L):
+    from codpiece_b200._lib import CpqTensor
+    w = CpqTensor()
+    w.type = 12
+    w.ne[:] = [5120, 4, 1, 1]
+    w.nb[:] = [144, 2880, 2880 * 4, 2880 * 4]
+    w.data = 0x1000
+    x = CpqTensor()
+    x.type = 0
+    x.ne[:] = [5120, 1, 1, 1]
+    x.nb[:] = [4, 20480, 20480, 20480]
+    x.data = 0x2000
+    y = CpqTensor()
+    y.type = 0
+    y.ne[:] = [4, 1, 1, 1]
+    y.nb[:] = [4, 16, 16, 16]
+    y.data = 0x3000
+    ws = C.c_void_p(0)
+    bad = CpqTensor.from_buffer_copy(w)
+    bad.type = 30  # BF16
+    assert L.cpq_mul_mat_ws(C.byref(bad), C.byref(x), C.byref(y), ws, 0, None) == 2
+    assert b"BF16" in L.cpq_last_error() or b"unknown" in L.cpq_last_error() or b"not Q4_K" in L.cpq_last_error()
+    bad = CpqTensor.from_buffer_copy(w)
+    bad.ne[3] = 2
+    assert L.cpq_mul_mat_ws(C.byref(bad), C.byref(x), C.byref(y), ws, 0, None) == 2
+    bady = CpqTensor.from_buffer_copy(y)
+    bady.ne[0] = 5
+    assert L.cpq_mul_mat_ws(C.byref(w), C.byref(x), C.byref(bady), ws, 0, None) == 1
+    # a valid request without workspace reports it instead of launching
+    assert L.cpq_mul_mat_ws(C.byref(w), C.byref(x), C.byref(y), ws, 0, None) == 3
+    # empty batch: success, nothing launched
+    x0 = CpqTensor.from_buffer_copy(x)
+    x0.ne[1] = 0
+    y0 = CpqTensor.from_buffer_copy(y)
+    y0.ne[1] = 0
+    assert L.cpq_mul_mat_ws(C.byref(w), C.byref(x0), C.byref(y0), ws, 0, None) == 0
+    assert L.cpq_mul_mat_workspace_size(C.byref(w), C.byref(x)) >= 5120 + 20 * 4 + 320 * 2
+
+
+def test_quantize_act_rejects_bad_shapes(L):
+    assert L.cpq_quantize_act(12, None, None, 100, 1, None) == 1   # K not a multiple of 256
+    assert L.cpq_quantize_act(30, None, None, 256, 1, None) == 2   # BF16 has no vec_dot_type here
+    assert L.cpq_quantize_act(12, None, None, 256, 0, None) == 0   # empty
