@@ -1,0 +1,140 @@
+// act_prep.cuh — produce the quantized activation image the decode GEMV reads.
+//
+// The row GEMV (gemv_row.cuh) pulls its activations into shared memory with
+// one bulk copy of this image:
+//   qs  [m][K]        int8 Q8_K quants, natural element order
+//   d   [m][nbk]      f32 Q8_K scales (padded to 16 bytes)
+//   bs  [m][nbk][16]  32-element sums split into low bytes (0-7) and high
+//                     bytes (8-15), the operands of the min-term dp4a
+// (row_act_bytes() gives the size, a multiple of 128).
+//
+// One warp per (token, 256-block), all blocks in one round across the GPU.
+// The input transform before quantization is one of the fused prologues of
+// codpiece's layer (qwen35.rs:2534-2537, 2777-2783):
+//   PLAIN   v = x
+//   RMS     v = rms_norm(x + r) * g   (r, g optional; x + r is also written
+//                                      out when h_out is given: the residual add)
+//   SWIGLU  v = silu(x) * r           (x = gate, r = up)
+// rms_norm follows ggml-cpu: sum of (x*x rounded to fp32) in double,
+// mean = sum/K as fp32, scale = 1/sqrt(mean + eps). Every CTA of a row
+// recomputes the row's sum itself (the row is a few KB), so no second pass
+// or grid-wide reduction is needed.
+#pragma once
+
+#include "q8k_block.cuh"
+
+namespace cpq {
+
+enum ActMode : int { kActPlain = 0, kActRms = 1, kActSwiglu = 2 };
+
+__host__ __device__ inline int row_act_bytes(int64_t k, int m) {
+    return int(align_up(align_up(size_t(m) * size_t(k), 16) + align_up(size_t(m) * size_t(k / kQK_K) * 4, 16) +
+                            size_t(m) * size_t(k / kQK_K) * 16,
+                        128));
+}
+
+struct ActPrepArgs {
+    int mode;
+    const float *x;    // [m][x_stride]
+    const float *r;    // residual (RMS) or up (SWIGLU); may be null for RMS
+    const float *g;    // RMS weight or null
+    float *h_out;      // RMS: x + r written here when non-null (must not alias x or r)
+    int64_t x_stride;  // floats between rows of x, r and h_out
+    int64_t k;
+    int m;
+    float eps;
+    uint8_t *out;      // the image (row_act_bytes(k, m) bytes)
+};
+
+// grid: (ceil(nbk / 8), m); block 256 = 8 warps, warp w quantizes block 8*blockIdx.x + w of token blockIdx.y
+__global__ void __launch_bounds__(256) act_prep_kernel(const ActPrepArgs a) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int t = blockIdx.y;
+    const int64_t k = a.k;
+    const int nbk = int(k / kQK_K);
+    const float *xr = a.x + t * a.x_stride;
+    const float *rr = a.r ? a.r + t * a.x_stride : nullptr;
+
+    float scale = 1.0f;
+    if (a.mode == kActRms) {
+        __shared__ double part[8];
+        double s = 0.0;
+        for (int64_t i = threadIdx.x; i < k; i += 256) {
+            const float v = rr ? __fadd_rn(xr[i], rr[i]) : xr[i];
+            s += double(__fmul_rn(v, v));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) part[warp] = s;
+        __syncthreads();
+        double tot = 0.0;
+#pragma unroll
+        for (int w = 0; w < 8; w++) tot += part[w];
+        const float mean = float(tot / double(k));
+        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+    }
+
+    const int b = blockIdx.x * 8 + warp;
+    if (b >= nbk) return;
+    const int64_t e0 = int64_t(b) * kQK_K + lane * 8;
+    float v[8];
+    {
+        const float4 x0 = *reinterpret_cast<const float4 *>(xr + e0);
+        const float4 x1 = *reinterpret_cast<const float4 *>(xr + e0 + 4);
+        v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+        v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+    }
+    if (a.mode == kActRms) {
+        if (rr) {
+            const float4 r0 = *reinterpret_cast<const float4 *>(rr + e0);
+            const float4 r1 = *reinterpret_cast<const float4 *>(rr + e0 + 4);
+            const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = __fadd_rn(v[e], rv[e]);
+            if (a.h_out) {
+                float *ho = a.h_out + t * a.x_stride + e0;
+                *reinterpret_cast<float4 *>(ho) = make_float4(v[0], v[1], v[2], v[3]);
+                *reinterpret_cast<float4 *>(ho + 4) = make_float4(v[4], v[5], v[6], v[7]);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = __fmul_rn(v[e], scale);
+        if (a.g) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = __fmul_rn(v[e], a.g[e0 + e]);
+        }
+    } else if (a.mode == kActSwiglu) {
+        const float4 u0 = *reinterpret_cast<const float4 *>(rr + e0);
+        const float4 u1 = *reinterpret_cast<const float4 *>(rr + e0 + 4);
+        const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const float s = __fdiv_rn(v[e], __fadd_rn(1.0f, expf(-v[e])));
+            v[e] = __fmul_rn(s, uv[e]);
+        }
+    }
+
+    int q[8];
+    const float d = q8k_quantize_block(v, lane, q);
+    uint32_t lo, hi;
+    pack8(q, lo, hi);
+    uint8_t *qs = a.out;
+    float *dd = reinterpret_cast<float *>(a.out + align_up(size_t(a.m) * size_t(k), 16));
+    uint8_t *bs = reinterpret_cast<uint8_t *>(dd) + align_up(size_t(a.m) * nbk * 4, 16);
+    *reinterpret_cast<uint2 *>(qs + t * k + e0) = make_uint2(lo, hi);
+    int s8 = 0;
+#pragma unroll
+    for (int e = 0; e < 8; e++) s8 += q[e];
+    int s32 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);
+    s32 += __shfl_xor_sync(0xffffffffu, s32, 2);
+    if ((lane & 3) == 0) {
+        uint8_t *bb = bs + (size_t(t) * nbk + b) * 16;
+        bb[lane >> 2] = uint8_t(s32 & 0xff);
+        bb[8 + (lane >> 2)] = uint8_t(int8_t(s32 >> 8));
+    }
+    if (lane == 0) dd[t * nbk + b] = d;
+}
+
+}  // namespace cpq

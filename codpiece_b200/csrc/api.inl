@@ -10,6 +10,7 @@
 #include <cstdlib>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 
 namespace cpq {
 
@@ -30,6 +31,15 @@ static cpq_status cuda_fail(cudaError_t e, const char *what) {
 }
 
 constexpr int kMaxDevices = 64;
+
+// Workspace carve-up: [row-block counters][per-warp partials][activations].
+// The counters must be zero before the first call; the MMA kernel leaves
+// them zero after every successful call.
+constexpr size_t kWsCounters = 65536;                       // row blocks per call (>= 1M rows)
+constexpr size_t kWsCountersBytes = kWsCounters * sizeof(int);
+constexpr size_t kWsMaxWarps = 148 * 2 * 16;                // persistent warps, generous
+constexpr size_t kWsPartialBytes = kWsMaxWarps * 2 * 16 * 16 * sizeof(float);
+constexpr size_t kWsActOffset = kWsCountersBytes + kWsPartialBytes;
 
 struct DevState {
     void *ws = nullptr;
@@ -248,11 +258,251 @@ static cudaError_t launch_gemv(const GemvArgs &a, int mt, cudaStream_t st) {
     }
 }
 
-constexpr int kGemvMaxTokens = 8;  // tokens per GEMV launch
+constexpr int kGemvMaxTokens = 8;  // tokens per GEMV launch (dp4a kernels)
+
+// Q4_K: fragment-order quantization, then the tensor-core GEMV per group of
+// up to 16 tokens.
+template <int NG>
+static cudaError_t launch_q4k_mma_t(MmaArgs &a, cudaStream_t st) {
+    auto kern = gemv_q4k_mma_kernel<NG>;
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    static std::atomic<int> occ[kMaxDevices];
+    int bpm = occ[dev].load(std::memory_order_relaxed);
+    if (bpm == 0) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaSmem);
+        if (e != cudaSuccess) return e;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bpm, kern, kMmaWarps * 32, kMmaSmem);
+        if (e != cudaSuccess) return e;
+        if (bpm < 1) bpm = 1;
+        occ[dev].store(bpm, std::memory_order_relaxed);
+    }
+    const int64_t T = a.mb_start[a.n_w] * a.nbk;
+    const int64_t cap = std::min<int64_t>(int64_t(sm_count(dev)) * bpm * kMmaWarps, int64_t(kWsMaxWarps));
+    a.n_warps = std::max<int64_t>(1, std::min<int64_t>(cap, T));
+    const int64_t grid = (a.n_warps + kMmaWarps - 1) / kMmaWarps;
+    return launch(kern, dim3(unsigned(grid)), dim3(kMmaWarps * 32), kMmaSmem, st, a);
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// link-time libcuda dependency). Maps depend only on (pointer, rows, row
+// stride, K), so they are cached.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return EncodeTiledFn(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+struct TmapKey {
+    const void *p;
+    int64_t n, k;
+    size_t rs;
+    int box_rows, box_sb;
+    bool operator==(const TmapKey &o) const {
+        return p == o.p && n == o.n && k == o.k && rs == o.rs && box_rows == o.box_rows && box_sb == o.box_sb;
+    }
+};
+struct TmapKeyHash {
+    size_t operator()(const TmapKey &t) const {
+        return std::hash<const void *>()(t.p) ^ (size_t(t.n) * 1000003u) ^ (size_t(t.k) << 20) ^ (t.rs << 7) ^
+               (size_t(t.box_rows) << 40) ^ (size_t(t.box_sb) << 48);
+    }
+};
+
+// Q4_K weight [n rows][rs bytes] as a 2-D u64 tensor; box = box_rows rows x box_sb superblocks.
+static cpq_status q4k_tensor_map(const uint8_t *w, int64_t n, int64_t k, size_t rs, CUtensorMap *out,
+                                 int box_rows = kMmaRows, int box_sb = kMmaSB) {
+    static std::mutex mu;
+    static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> cache;
+    const TmapKey key{w, n, k, rs, box_rows, box_sb};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *out = it->second;
+            return CPQ_SUCCESS;
+        }
+    }
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return fail(CPQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {cuuint64_t(k / kQK_K) * (kQ4K_Bytes / 8), cuuint64_t(n)};
+    const cuuint64_t strides[1] = {cuuint64_t(rs)};
+    const cuuint32_t box[2] = {cuuint32_t(box_sb * (kQ4K_Bytes / 8)), cuuint32_t(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUtensorMap m;
+    const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t *>(w), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(CPQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    std::lock_guard<std::mutex> lk(mu);
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, m);
+    *out = m;
+    return CPQ_SUCCESS;
+}
+
+// Activation region bytes (the largest of the three layouts) and the fp32
+// prologue region that follows it.
+static size_t act_region_bytes(int32_t vt, int64_t k, int64_t m);
+static size_t ws_need(int32_t vt, int64_t k, int64_t m) {
+    return kWsActOffset + act_region_bytes(vt, k, m) + align_up(size_t(m) * size_t(k) * 4, 256);
+}
+
+// Bytes of the fragment-order activation region for one group of mp tokens.
+static size_t frag_bytes(int64_t k, int mp) {
+    const size_t nbk = size_t(k / kQK_K);
+    return align_up(nbk * mp * 256, 256) + align_up(nbk * mp * 16, 256) + align_up(nbk * mp * 4, 256);
+}
+
+constexpr int kSmemMax = 227 * 1024;
+
+static int row_smem_bytes(int64_t k, int mt) { return kRowBarBytes + row_act_bytes(k, mt) + kRowRingBytes; }
+
+template <int MT>
+static cudaError_t launch_q4k_row_t(RowArgs &a, int smem, cudaStream_t st) {
+    auto kern = gemv_q4k_row_kernel<MT>;
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    static std::atomic<int> set[kMaxDevices];
+    if (!set[dev].load(std::memory_order_relaxed)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        if (e != cudaSuccess) return e;
+        set[dev].store(1, std::memory_order_relaxed);
+    }
+    const int64_t T = a.mb_start[a.n_w] * a.nbk;
+    const int64_t cap = std::min<int64_t>(int64_t(sm_count(dev)) * kRowWarps, int64_t(kWsMaxWarps));
+    a.n_warps = std::max<int64_t>(1, std::min<int64_t>(cap, T));
+    const int64_t grid = (a.n_warps + kRowWarps - 1) / kRowWarps;
+    return launch(kern, dim3(unsigned(grid)), dim3(kRowWarps * 32), size_t(smem), st, a);
+}
+
+// M <= 3: the activation image is built by act_prep_kernel (with the fused
+// prologue), then the row GEMV pulls it in with one bulk copy.
+static cpq_status run_q4k_row(const GemvArgs &g, const float *x, int64_t x_stride, int m, const cpq_prologue &pro,
+                              uint8_t *ws, cudaStream_t st) {
+    static thread_local RowArgs a;
+    std::memset(&a, 0, sizeof a);
+    const int64_t k = g.k;
+    a.n_w = g.n_w;
+    for (int i = 0; i < g.n_w; i++) {
+        a.n[i] = g.row_start[i + 1] - g.row_start[i];
+        a.y[i] = g.y[i];
+        a.y_stride[i] = g.y_stride[i];
+        a.mb_start[i + 1] = a.mb_start[i] + (a.n[i] + kRowRows - 1) / kRowRows;
+        if (a.n[i] > 0) {
+            cpq_status rc = q4k_tensor_map(g.w[i], a.n[i], k, g.rs, &a.tmap[i], kRowRows, 1);
+            if (rc) return rc;
+        }
+    }
+    if (a.mb_start[g.n_w] > int64_t(kWsCounters))
+        return fail(CPQ_ERR_UNSUPPORTED, "too many row blocks (%lld) for the workspace counters",
+                    (long long)a.mb_start[g.n_w]);
+    uint8_t *act = ws + kWsActOffset;
+    ActPrepArgs pa;
+    pa.mode = pro.mode;
+    pa.x = x;
+    pa.r = pro.r;
+    pa.g = pro.g;
+    pa.h_out = pro.h_out;
+    pa.x_stride = x_stride;
+    pa.k = k;
+    pa.m = m;
+    pa.eps = pro.eps;
+    pa.out = act;
+    const int nbk = int(k / kQK_K);
+    cudaError_t e = launch(act_prep_kernel, dim3(unsigned((nbk + 7) / 8), unsigned(m)), dim3(256), 0, st, pa);
+    if (e != cudaSuccess) return cuda_fail(e, "act_prep launch");
+    a.nbk = nbk;
+    a.m = m;
+    a.act = act;
+    a.partials = reinterpret_cast<float *>(ws + kWsCountersBytes);
+    a.counters = reinterpret_cast<int *>(ws);
+    const int smem = row_smem_bytes(k, m);
+    switch (m) {
+    case 1: e = launch_q4k_row_t<1>(a, smem, st); break;
+    case 2: e = launch_q4k_row_t<2>(a, smem, st); break;
+    default: e = launch_q4k_row_t<3>(a, smem, st); break;
+    }
+    return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "q4_K row gemv launch");
+}
+
+static size_t act_region_bytes(int32_t vt, int64_t k, int64_t m) {
+    size_t b = act_layout(vt, k, std::max<int64_t>(m, 1)).bytes;
+    if (vt == CPQ_TYPE_Q8_K) {
+        b = std::max(b, frag_bytes(k, 16));
+        b = std::max(b, size_t(row_act_bytes(k, kRowMaxTokens)));
+    }
+    return align_up(b, 256);
+}
+
+static cpq_status run_q4k_mma(const GemvArgs &g, const float *x, int64_t x_stride, int64_t m, uint8_t *ws,
+                              cudaStream_t st) {
+    const int64_t k = g.k, nbk = k / kQK_K;
+    static thread_local MmaArgs a;  // large (tensor maps); filled per call
+    std::memset(&a, 0, sizeof a);
+    a.n_w = g.n_w;
+    a.mb_start[0] = 0;
+    for (int i = 0; i < g.n_w; i++) {
+        a.n[i] = g.row_start[i + 1] - g.row_start[i];
+        a.y_stride[i] = g.y_stride[i];
+        a.mb_start[i + 1] = a.mb_start[i] + (a.n[i] + kMmaRows - 1) / kMmaRows;
+        if (a.n[i] > 0) {
+            cpq_status rc = q4k_tensor_map(g.w[i], a.n[i], k, g.rs, &a.tmap[i]);
+            if (rc) return rc;
+        }
+    }
+    if (a.mb_start[g.n_w] > int64_t(kWsCounters))
+        return fail(CPQ_ERR_UNSUPPORTED, "too many row blocks (%lld) for the workspace counters",
+                    (long long)a.mb_start[g.n_w]);
+    a.nbk = int(nbk);
+    a.partials = reinterpret_cast<float *>(ws + kWsCountersBytes);
+    a.counters = reinterpret_cast<int *>(ws);
+
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return fail(CPQ_ERR_CUDA, "no current device");
+    uint8_t *act = ws + kWsActOffset;
+    for (int64_t t0 = 0; t0 < m; t0 += kMmaMaxTokens) {
+        const int mt = int(std::min<int64_t>(kMmaMaxTokens, m - t0));
+        const int mp = mt <= 8 ? 8 : 16;
+        int8_t *qs = reinterpret_cast<int8_t *>(act);
+        uint8_t *bs = act + align_up(size_t(nbk) * mp * 256, 256);
+        float *d = reinterpret_cast<float *>(bs + align_up(size_t(nbk) * mp * 16, 256));
+        const int64_t qwarps = nbk * mp;
+        cudaError_t e = launch(quantize_q8K_frag_kernel, dim3(unsigned(std::min<int64_t>((qwarps + 7) / 8, 65535))),
+                               dim3(256), 0, st, x + t0 * x_stride, k, mt, mp, x_stride, qs, bs, d);
+        if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+        a.m = mt;
+        a.act.qs = qs;
+        a.act.bs = bs;
+        a.act.d = d;
+        a.act.mp = mp;
+        for (int i = 0; i < g.n_w; i++) a.y[i] = g.y[i] + t0 * g.y_stride[i];
+        e = mt <= 8 ? launch_q4k_mma_t<1>(a, st) : launch_q4k_mma_t<2>(a, st);
+        if (e != cudaSuccess) return cuda_fail(e, "q4_K gemv launch");
+    }
+    return CPQ_SUCCESS;
+}
 
 // Quantize X once into the workspace, then run every weight against it.
 static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
-                               void *ws, size_t ws_bytes, cudaStream_t st) {
+                               const cpq_prologue *pro_in, void *ws, size_t ws_bytes, cudaStream_t st) {
+    cpq_prologue pro = {CPQ_PRO_NONE, nullptr, nullptr, nullptr, 0.0f};
+    if (pro_in) pro = *pro_in;
+    if (pro.mode != CPQ_PRO_NONE && pro.mode != CPQ_PRO_RMS && pro.mode != CPQ_PRO_SWIGLU)
+        return fail(CPQ_ERR_INVALID_ARG, "prologue mode %d", int(pro.mode));
+    if (pro.mode == CPQ_PRO_SWIGLU && !pro.r) return fail(CPQ_ERR_INVALID_ARG, "SWIGLU prologue needs r (up)");
+    if ((pro.r && !aligned(pro.r, 16)) || (pro.h_out && !aligned(pro.h_out, 16)))
+        return fail(CPQ_ERR_UNSUPPORTED, "prologue r/h_out must be 16-byte aligned");
     if (n_w < 1 || n_w > kMaxMulti) return fail(CPQ_ERR_INVALID_ARG, "n_w=%d must be in 1..%d", n_w, kMaxMulti);
     if (!w || !y) return fail(CPQ_ERR_INVALID_ARG, "weight/output arrays are null");
     MMShape s0;
@@ -281,14 +531,33 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
     const int32_t vt = vec_dot_type(s0.wtype);
     const ActLayout L = act_layout(vt, s0.k, m);
     if (!ws) return fail(CPQ_ERR_NOT_INITIALIZED, "no workspace (call cpq_init on this device first)");
-    if (ws_bytes < L.bytes) return fail(CPQ_ERR_WORKSPACE, "workspace %zu B < %zu B needed", ws_bytes, L.bytes);
+    if (ws_bytes < ws_need(vt, s0.k, m))
+        return fail(CPQ_ERR_WORKSPACE, "workspace %zu B < %zu B needed", ws_bytes, ws_need(vt, s0.k, m));
     if (!aligned(ws, 256)) return fail(CPQ_ERR_INVALID_ARG, "workspace must be 256-byte aligned");
+    uint8_t *wsb = static_cast<uint8_t *>(ws);
+    const float *xp = static_cast<const float *>(x->data);
+    int64_t x_stride = int64_t(x->nb[1] / 4);
 
-    cudaError_t e = launch_quantize(vt, static_cast<const float *>(x->data), s0.k, m, int64_t(x->nb[1] / 4), ws, L,
-                                    nullptr, st);
+    cudaError_t e;
+    if (s0.wtype == CPQ_TYPE_Q4_K && m <= kRowMaxTokens && row_smem_bytes(s0.k, int(m)) <= kSmemMax)
+        return run_q4k_row(a, xp, x_stride, int(m), pro, wsb, st);
+
+    if (pro.mode != CPQ_PRO_NONE) {
+        // the other paths quantize an fp32 input: apply the prologue into the workspace first
+        float *tmp = reinterpret_cast<float *>(wsb + kWsActOffset + act_region_bytes(vt, s0.k, m));
+        e = launch(prologue_f32_kernel, dim3(unsigned(m)), dim3(256), 0, st, int(pro.mode), xp, pro.r, pro.g,
+                   pro.h_out, x_stride, s0.k, pro.eps, tmp);
+        if (e != cudaSuccess) return cuda_fail(e, "prologue launch");
+        xp = tmp;
+        x_stride = s0.k;
+    }
+    if (s0.wtype == CPQ_TYPE_Q4_K) return run_q4k_mma(a, xp, x_stride, m, wsb, st);
+
+    void *act_ws = wsb + kWsActOffset;
+    e = launch_quantize(vt, xp, s0.k, m, x_stride, act_ws, L, nullptr, st);
     if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
 
-    const uint8_t *base = static_cast<const uint8_t *>(ws);
+    const uint8_t *base = static_cast<const uint8_t *>(act_ws);
     const int64_t blk = type_blck(vt);
     for (int64_t t0 = 0; t0 < m; t0 += kGemvMaxTokens) {
         const int mt = int(std::min<int64_t>(kGemvMaxTokens, m - t0));
@@ -298,7 +567,6 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
         g.act.bsums = reinterpret_cast<const int16_t *>(base + L.bs_off) + t0 * (s0.k / 16);
         for (int i = 0; i < n_w; i++) g.y[i] = a.y[i] + t0 * a.y_stride[i];
         switch (s0.wtype) {
-        case CPQ_TYPE_Q4_K: e = launch_gemv<FmtQ4K>(g, mt, st); break;
         case CPQ_TYPE_Q6_K: e = launch_gemv<FmtQ6K>(g, mt, st); break;
         default: e = launch_gemv<FmtQ8_0>(g, mt, st); break;
         }
@@ -362,10 +630,13 @@ cpq_status cpq_init(int device, size_t workspace_bytes) {
         ds.ws = nullptr;
         ds.ws_bytes = 0;
     }
-    const size_t bytes = std::max<size_t>(workspace_bytes, 256);
+    const size_t bytes = std::max<size_t>(workspace_bytes, kWsActOffset + 256);
     e = cudaMalloc(&ds.ws, bytes);
+    if (e == cudaSuccess) e = cudaMemset(ds.ws, 0, kWsActOffset);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     cudaSetDevice(prev);
     if (e != cudaSuccess) {
+        if (ds.ws) cudaFree(ds.ws);
         ds.ws = nullptr;
         return cuda_fail(e, "cudaMalloc(workspace)");
     }
@@ -393,12 +664,12 @@ size_t cpq_mul_mat_workspace_size(const cpq_tensor *w, const cpq_tensor *x) {
     if (!w || !x) return 0;
     const int32_t vt = vec_dot_type(w->type);
     if (vt < 0 || x->ne[1] < 0 || w->ne[0] <= 0) return 0;
-    return act_layout(vt, w->ne[0], std::max<int64_t>(x->ne[1], 1)).bytes;
+    return ws_need(vt, w->ne[0], std::max<int64_t>(x->ne[1], 1));
 }
 
 cpq_status cpq_mul_mat_ws(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *y, void *workspace,
                           size_t workspace_bytes, void *stream) {
-    return mul_mat_core(&w, &y, 1, x, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+    return mul_mat_core(&w, &y, 1, x, nullptr, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 cpq_status cpq_mul_mat(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *y, void *stream) {
@@ -406,7 +677,7 @@ cpq_status cpq_mul_mat(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *y, 
     size_t bytes;
     cpq_status rc = workspace_of_current(&ws, &bytes);
     if (rc) return rc;
-    return mul_mat_core(&w, &y, 1, x, ws, bytes, static_cast<cudaStream_t>(stream));
+    return mul_mat_core(&w, &y, 1, x, nullptr, ws, bytes, static_cast<cudaStream_t>(stream));
 }
 
 cpq_status cpq_mul_mat_multi(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
@@ -415,7 +686,16 @@ cpq_status cpq_mul_mat_multi(const cpq_tensor *const *w, cpq_tensor *const *y, i
     size_t bytes;
     cpq_status rc = workspace_of_current(&ws, &bytes);
     if (rc) return rc;
-    return mul_mat_core(w, y, n_w, x, ws, bytes, static_cast<cudaStream_t>(stream));
+    return mul_mat_core(w, y, n_w, x, nullptr, ws, bytes, static_cast<cudaStream_t>(stream));
+}
+
+cpq_status cpq_mul_mat_fused(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
+                             const cpq_prologue *pro, void *stream) {
+    void *ws;
+    size_t bytes;
+    cpq_status rc = workspace_of_current(&ws, &bytes);
+    if (rc) return rc;
+    return mul_mat_core(w, y, n_w, x, pro, ws, bytes, static_cast<cudaStream_t>(stream));
 }
 
 cpq_status cpq_quantize_act(int32_t wtype, const float *x, void *out, int64_t k, int64_t m, void *stream) {

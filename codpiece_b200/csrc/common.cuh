@@ -141,6 +141,13 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
     return d;
 }
 
+// dot of 4 unsigned bytes (a) with 4 unsigned bytes (b), plus c.
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 // 16 bytes from shared memory at a 2-byte aligned address: five aligned
 // words and a funnel shift (shift 0 when the address is 4-byte aligned).
 __device__ __forceinline__ uint4 lds16_a2(const uint8_t *p) {

@@ -38,6 +38,49 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float *__restrict__
     }
 }
 
+// The fp32 form of the fused prologues (act_prep.cuh) for paths that
+// quantize separately: RMS  out = rms_norm(x + r) * g  (h_out = x + r when
+// given);  SWIGLU  out = silu(x) * r. One CTA per row; out is [m][k] dense.
+__global__ void __launch_bounds__(256) prologue_f32_kernel(int mode, const float *__restrict__ x,
+                                                           const float *__restrict__ r, const float *__restrict__ g,
+                                                           float *__restrict__ h_out, int64_t x_stride, int64_t k,
+                                                           float eps, float *__restrict__ out) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int64_t row = blockIdx.x;
+    const float *xr = x + row * x_stride;
+    const float *rr = r ? r + row * x_stride : nullptr;
+    float *orow = out + row * k;
+    if (mode == 2) {  // SWIGLU
+        for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+            const float gv = xr[i];
+            const float s = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
+            orow[i] = __fmul_rn(s, rr[i]);
+        }
+        return;
+    }
+    __shared__ double part[8];
+    double s = 0.0;
+    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+        const float v = rr ? __fadd_rn(xr[i], rr[i]) : xr[i];
+        if (h_out) h_out[row * x_stride + i] = v;
+        s += double(__fmul_rn(v, v));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    double tot = 0.0;
+    for (int w = 0; w < int(blockDim.x >> 5); w++) tot += part[w];
+    const float mean = float(tot / double(k));
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+        const float v0 = rr ? __fadd_rn(xr[i], rr[i]) : xr[i];
+        const float v = __fmul_rn(v0, scale);
+        orow[i] = g ? __fmul_rn(v, g[i]) : v;
+    }
+}
+
 // ggml silu(x) = x / (1 + exp(-x)); act = silu(gate) * up.
 __global__ void swiglu_kernel(const float *__restrict__ gate, const float *__restrict__ up, float *__restrict__ act,
                               int64_t n) {

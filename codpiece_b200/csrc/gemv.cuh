@@ -22,7 +22,17 @@
 
 namespace cpq {
 
-constexpr int kGemvWarps = 8;  // warps per CTA
+#ifndef CPQ_GEMV_WARPS
+#define CPQ_GEMV_WARPS 8
+#endif
+#ifndef CPQ_Q4K_PASSES
+#define CPQ_Q4K_PASSES 2
+#endif
+#ifndef CPQ_Q4K_STAGES
+#define CPQ_Q4K_STAGES 6
+#endif
+
+constexpr int kGemvWarps = CPQ_GEMV_WARPS;  // warps per CTA
 constexpr int kMaxMulti = 4;   // weights sharing one activation in one launch
 
 struct GemvArgs {
@@ -44,10 +54,10 @@ struct GemvArgs {
 
 struct FmtQ4K {
     static constexpr int kBlkBytes = kQ4K_Bytes, kBlkElems = kQK_K;
-    static constexpr int kPasses = 2;               // 4 blocks per pass, 8 lanes each
+    static constexpr int kPasses = CPQ_Q4K_PASSES;  // 4 blocks per pass, 8 lanes each
     static constexpr int kCB = 4 * kPasses;         // blocks per chunk
     static constexpr int kStageBytes = kCB * kBlkBytes;  // 144 B blocks keep 16 B alignment
-    static constexpr int kStages = 6;
+    static constexpr int kStages = CPQ_Q4K_STAGES;
     static constexpr bool kAligned = true;
 
     template <int MT>

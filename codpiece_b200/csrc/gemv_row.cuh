@@ -1,0 +1,244 @@
+// gemv_row.cuh — Q4_K x Q8_K decode GEMV (M = 1..3), one lane per weight row.
+//
+// Same arithmetic as ggml_vec_dot_q4_K_q8_K: exact integer sub-block dots
+// (dp4a), six-bit scales and mins applied as integers, fp32 per superblock.
+//
+// Layout. A warp owns 32 consecutive rows and walks K one superblock at a
+// time; lane r holds row r's 144-byte block in registers (9 x 16-byte shared
+// loads; the dense 144-byte pitch written by the TMA puts 8 consecutive rows
+// in distinct bank groups, so the loads are conflict-free) and dots it with
+// the activation block, which every lane reads from the same shared address
+// (broadcast). Per 256 weights a lane spends ~200 instructions, ~6 warp
+// instructions per block, against ~25 that the HBM stream leaves room for.
+//
+// Activations. The quantized activation image (act_prep.cuh, a few KB) is
+// pulled into shared memory with one bulk copy right after
+// griddepcontrol.wait; the weight stages were issued before that wait, so
+// under programmatic dependent launch the weight stream overlaps the
+// producer of the activations.
+//
+// Memory path and work split are those of gemv_mma.cuh: a private ring of
+// 2-D TMA tensor copies per warp (box 32 rows x 1 superblock, no multicast)
+// and a stream-K split of (32-row block, superblock) iterations with a
+// deterministic last-arriver fix-up.
+#pragma once
+
+#include "act_prep.cuh"
+#include "gemv_mma.cuh"
+
+namespace cpq {
+
+#ifndef CPQ_ROW_WARPS
+#define CPQ_ROW_WARPS 8
+#endif
+#ifndef CPQ_ROW_STAGES
+#define CPQ_ROW_STAGES 4
+#endif
+
+constexpr int kRowWarps = CPQ_ROW_WARPS;
+constexpr int kRowStages = CPQ_ROW_STAGES;
+constexpr int kRowRows = 32;
+constexpr int kRowStageBytes = kRowRows * kQ4K_Bytes;  // one superblock of 32 rows
+constexpr int kRowBarBytes = 128 * ((kRowWarps * kRowStages * 8 + 8 + 127) / 128);  // + the activation barrier
+constexpr int kRowRingBytes = kRowWarps * kRowStages * kRowStageBytes;
+constexpr int kRowMaxTokens = 3;
+static_assert(kQ4K_Bytes % 128 == 16, "per-lane 16-byte row loads must hit distinct bank groups");
+
+struct alignas(64) RowArgs {
+    CUtensorMap tmap[4];  // weight i as [n rows][row bytes / 8] u64, box 32 x 18 (one superblock)
+    float *y[4];
+    int64_t n[4];
+    int64_t y_stride[4];
+    int64_t mb_start[5];  // prefix sums of 32-row blocks per weight
+    int n_w;
+    int nbk;
+    int m;                // tokens (1..3)
+    const uint8_t *act;   // activation image (act_prep.cuh), row_act_bytes(K, m) bytes
+    int64_t n_warps;
+    float *partials;      // [warp][2 segments][256 floats]
+    int *counters;        // [row block], zero between calls
+};
+
+template <int MT>
+__global__ void __launch_bounds__(kRowWarps * 32, 1) gemv_q4k_row_kernel(const __grid_constant__ RowArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nbk = a.nbk;
+    const int64_t k = int64_t(nbk) * kQK_K;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * kRowStages;
+    uint64_t *act_bar = reinterpret_cast<uint64_t *>(smem) + kRowWarps * kRowStages;
+    int8_t *xs = reinterpret_cast<int8_t *>(smem + kRowBarBytes);
+    float *xd = reinterpret_cast<float *>(smem + kRowBarBytes + align_up(size_t(MT) * size_t(k), 16));
+    uint8_t *xb = reinterpret_cast<uint8_t *>(xd) + align_up(size_t(MT) * nbk * 4, 16);
+    uint8_t *ring = smem + kRowBarBytes + row_act_bytes(k, MT) + warp * kRowStages * kRowStageBytes;
+    if (lane == 0) {
+#pragma unroll
+        for (int s = 0; s < kRowStages; s++) mbar_init(&bars[s], 1);
+        if (warp == 0) mbar_init(act_bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    const int64_t T = a.mb_start[a.n_w] * nbk;
+    const int64_t G = a.n_warps;
+    const int64_t g = int64_t(blockIdx.x) * kRowWarps + warp;
+    const bool active = g < G;
+    const int64_t it_begin = active ? g * T / G : 0, it_end = active ? (g + 1) * T / G : 0;
+    const uint64_t policy = l2_policy_evict_first();
+
+    auto weight_of = [&](int64_t mb) {
+        int wi = 0;
+#pragma unroll
+        for (int q = 1; q < 4; q++)
+            if (q < a.n_w && mb >= a.mb_start[q]) wi = q;
+        return wi;
+    };
+
+    int64_t p_it = it_begin, p_mb = it_begin / nbk;
+    int p_kb = int(it_begin - p_mb * nbk);
+    auto issue = [&](int slot) {
+        if (lane == 0) {
+            const int wi = weight_of(p_mb);
+            const int row0 = int((p_mb - a.mb_start[wi]) * kRowRows);
+            mbar_arrive_expect_tx(&bars[slot], kRowStageBytes);
+            tma_load_2d(ring + slot * kRowStageBytes, &a.tmap[wi], p_kb * (kQ4K_Bytes / 8), row0, &bars[slot], policy);
+        }
+        p_it++;
+        if (++p_kb == nbk) {
+            p_kb = 0;
+            p_mb++;
+        }
+    };
+    for (int j = 0; j < kRowStages && p_it < it_end; j++) issue(j);
+
+    // ---- activations: one bulk copy of the image the previous kernel wrote ----
+    pdl_wait();
+    const uint32_t act_bytes = uint32_t(row_act_bytes(k, MT));
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(act_bar, act_bytes);
+        bulk_g2s(xs, a.act, act_bytes, act_bar);
+    }
+    if (!mbar_wait_bounded(act_bar, 0)) {
+        // error recorded in the device word: wait (bounded) for this warp's weight copies, then leave
+        for (int64_t j = 0; j < p_it - it_begin; j++) mbar_wait_bounded(&bars[j], 0);
+        return;
+    }
+    pdl_launch_dependents();
+    if (!active) return;
+
+    float acc[MT];
+#pragma unroll
+    for (int t = 0; t < MT; t++) acc[t] = 0.0f;
+    int64_t c_it = it_begin, c_mb = it_begin / nbk;
+    int c_kb = int(it_begin - c_mb * nbk);
+    int64_t seg_start = it_begin;
+    int slot = 0;
+    uint32_t phase = 0;
+    while (c_it < it_end) {
+        if (!mbar_wait_bounded(&bars[slot], phase)) {
+            // error recorded in the device word: wait (bounded) for this warp's other copies, then leave
+            for (int k2 = 1; k2 < kRowStages && p_it > c_it + k2; k2++)
+                mbar_wait_bounded(&bars[(slot + k2) % kRowStages], phase ^ uint32_t(slot + k2 >= kRowStages));
+            return;
+        }
+        __syncwarp();
+        const uint8_t *blk = ring + slot * kRowStageBytes + lane * kQ4K_Bytes;
+        const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+        uint4 qv[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) qv[i] = *reinterpret_cast<const uint4 *>(blk + 16 + 16 * i);
+        __syncwarp();
+        if (p_it < it_end) issue(slot);  // the stage is in registers: refill it now
+
+        const uint32_t sca = h.y & 0x3f3f3f3fu, scb = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
+        const uint32_t mna = h.z & 0x3f3f3f3fu, mnb = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
+        const float dw = half_bits_to_float(h.x), dm = half_bits_to_float(h.x >> 16);
+        int isc[MT];
+#pragma unroll
+        for (int t = 0; t < MT; t++) isc[t] = 0;
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+            const uint4 wa = qv[2 * jj], wb = qv[2 * jj + 1];
+            const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+            const uint32_t sw = jj < 2 ? sca : scb;
+            const int slo = byte_of(sw, (2 * jj) & 3), shi = byte_of(sw, (2 * jj + 1) & 3);
+#pragma unroll
+            for (int t = 0; t < MT; t++) {
+                const int4 *xp = reinterpret_cast<const int4 *>(xs + t * k + c_kb * kQK_K + 64 * jj);
+                const int4 x0 = xp[0], x1 = xp[1], x2 = xp[2], x3 = xp[3];
+                const int xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                const int xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+                int dl = 0, dh = 0;
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    dl = __dp4a(int(w[i] & 0x0f0f0f0fu), xl[i], dl);
+                    dh = dp4a_us(w[i] & 0xf0f0f0f0u, xh[i], dh);  // 16 * q_hi
+                }
+                isc[t] += slo * dl + shi * (dh >> 4);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < MT; t++) {
+            const uint4 bsv = *reinterpret_cast<const uint4 *>(xb + (size_t(t) * nbk + c_kb) * 16);
+            const int imn = 256 * (__dp4a(int(mna), int(bsv.z), 0) + __dp4a(int(mnb), int(bsv.w), 0)) +
+                            dp4a_uu(mna, bsv.x, dp4a_uu(mnb, bsv.y, 0));
+            const float dx = xd[t * nbk + c_kb];
+            acc[t] += (dw * dx) * float(isc[t]) - (dm * dx) * float(imn);
+        }
+
+        c_it++;
+        if (++slot == kRowStages) {
+            slot = 0;
+            phase ^= 1u;
+        }
+        const bool blk_end = (++c_kb == nbk);
+        if (blk_end || c_it == it_end) {
+            const int wi = weight_of(c_mb);
+            const int64_t row0 = (c_mb - a.mb_start[wi]) * kRowRows;
+            const bool row_ok = row0 + lane < a.n[wi];
+            if (seg_start == c_mb * nbk && blk_end) {
+#pragma unroll
+                for (int t = 0; t < MT; t++)
+                    if (t < a.m && row_ok) a.y[wi][size_t(t) * a.y_stride[wi] + row0 + lane] = acc[t];
+            } else {
+                const int64_t first = owner_warp(c_mb * nbk, G, T);
+                const int64_t last = owner_warp(c_mb * nbk + nbk - 1, G, T);
+                const int npieces = int(last - first + 1);
+                const int my_slot = (c_mb == it_begin / nbk) ? 0 : 1;
+                float *pp = a.partials + (size_t(g) * 2 + my_slot) * 256;
+#pragma unroll
+                for (int t = 0; t < MT; t++) pp[lane * 4 + t] = acc[t];
+                __syncwarp();
+                int old = 0;
+                if (lane == 0) old = atom_add_acq_rel_gpu(&a.counters[c_mb], 1);
+                old = __shfl_sync(0xffffffffu, old, 0);
+                __syncwarp();
+                if (old == npieces - 1) {
+                    float sum[MT];
+#pragma unroll
+                    for (int t = 0; t < MT; t++) sum[t] = 0.0f;
+                    for (int p = 0; p < npieces; p++) {
+                        const int64_t gp = first + p;
+                        const int sl = (c_mb == (gp * T / G) / nbk) ? 0 : 1;
+                        const volatile float *q = a.partials + (size_t(gp) * 2 + sl) * 256;
+#pragma unroll
+                        for (int t = 0; t < MT; t++) sum[t] += q[lane * 4 + t];
+                    }
+#pragma unroll
+                    for (int t = 0; t < MT; t++)
+                        if (t < a.m && row_ok) a.y[wi][size_t(t) * a.y_stride[wi] + row0 + lane] = sum[t];
+                    if (lane == 0) a.counters[c_mb] = 0;
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < MT; t++) acc[t] = 0.0f;
+            seg_start = c_it;
+            if (blk_end) {
+                c_kb = 0;
+                c_mb++;
+            }
+        }
+    }
+}
+
+}  // namespace cpq

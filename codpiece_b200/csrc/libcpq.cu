@@ -3,7 +3,11 @@
 // One TU keeps the per-device error word a plain __device__ variable without
 // relocatable device code. Parts:
 //   quantize.cuh     activation re-quantization (Q8_K, Q8_0), bit-exact
-//   gemv.cuh         small-M fused dequant GEMV/GEMM (TMA bulk-copy ring)
+//   gemv.cuh         small-M fused dequant GEMV/GEMM, dp4a (Q6_K, Q8_0)
+//   q8k_block.cuh    the Q8_K block quantizer shared by every Q8_K producer
+//   gemv_mma.cuh     Q4_K verify GEMM (M 4..16) on int8 mma tiles, stream-K
+//   act_prep.cuh     decode activation image: fused rms/swiglu prologue + Q8_K
+//   gemv_row.cuh     Q4_K decode GEMV (M 1..3), lane per row
 //   elementwise.cuh  rms norm, SwiGLU, residual add, argmax
 //   synth.cuh        seeded synthetic weights
 //   split.inl        tensor-parallel partition rules (host)
@@ -21,6 +25,9 @@
 #include "common.cuh"
 #include "elementwise.cuh"
 #include "gemv.cuh"
+#include "gemv_mma.cuh"
+#include "act_prep.cuh"
+#include "gemv_row.cuh"
 #include "quantize.cuh"
 #include "synth.cuh"
 #include "split.inl"

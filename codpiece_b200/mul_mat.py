@@ -18,7 +18,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import CpqTensor, check, lib
+from ._lib import PRO_NONE, PRO_RMS, PRO_SWIGLU, CpqPrologue, CpqTensor, check, lib
 
 TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_K = (
     _lib.TYPE_F32, _lib.TYPE_Q8_0, _lib.TYPE_Q4_K, _lib.TYPE_Q6_K, _lib.TYPE_Q8_K)
@@ -150,6 +150,31 @@ def mul_mat_multi(ws: list[QTensor], x: torch.Tensor, outs: list[torch.Tensor] |
     warr = (C.POINTER(CpqTensor) * n)(*[C.pointer(d) for d in wds])
     yarr = (C.POINTER(CpqTensor) * n)(*[C.pointer(d) for d in yds])
     check(lib().cpq_mul_mat_multi(warr, yarr, n, C.byref(xd), _stream(stream)), "cpq_mul_mat_multi")
+    return outs
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def mul_mat_fused(ws: list[QTensor], x: torch.Tensor, outs: list[torch.Tensor] | None = None, *, mode: int = PRO_NONE,
+                  r: torch.Tensor | None = None, g: torch.Tensor | None = None, h_out: torch.Tensor | None = None,
+                  eps: float = 1e-6, stream=None) -> list[torch.Tensor]:
+    """Y_i = W_i x quantize(f(X)) with f the fused prologue (include/cpq.h cpq_prologue):
+    PRO_RMS: rms_norm(X + r) * g (X + r stored to h_out when given); PRO_SWIGLU: silu(X) * r."""
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    if outs is None:
+        outs = [torch.empty(x.shape[0], w.n, dtype=torch.float32, device=x.device) for w in ws]
+    _ensure_workspace(ws[0], x)
+    wds = [w.desc() for w in ws]
+    yds = [f32_desc(o) for o in outs]
+    xd = f32_desc(x)
+    n = len(ws)
+    warr = (C.POINTER(CpqTensor) * n)(*[C.pointer(d) for d in wds])
+    yarr = (C.POINTER(CpqTensor) * n)(*[C.pointer(d) for d in yds])
+    pro = CpqPrologue(mode, _ptr(r), _ptr(g), _ptr(h_out), eps)
+    check(lib().cpq_mul_mat_fused(warr, yarr, n, C.byref(xd), C.byref(pro), _stream(stream)), "cpq_mul_mat_fused")
     return outs
 
 

@@ -119,7 +119,8 @@ class Stack:
         qmax = max((s.q[rank][1] - s.q[rank][0]) for s in self.shards) or 1
         kmax = max((s.k[rank][1] - s.k[rank][0]) for s in self.shards) or 1
         fmax = max((s.gate[rank][1] - s.gate[rank][0]) for s in self.shards) or 1
-        self.h, self.xn = f(e), f(e)
+        self.h, self.h_alt, self.xn = f(e), f(e), f(e)
+        self.h_final = self.h
         self.qb, self.kb, self.vb = f(qmax), f(kmax), f(kmax)
         self.part = f(e)
         self.gb, self.ub, self.act = f(fmax), f(fmax), f(fmax)
@@ -137,17 +138,27 @@ class Stack:
         return n + (self.head.nbytes if self.head is not None else 0)
 
     def launches_per_step(self) -> int:
-        """libcpq kernels one step launches (NCCL's own kernels not counted)."""
+        """libcpq kernels one step launches (NCCL's and torch's own kernels not counted)."""
+        m = self.m
+
+        def fused(qtype: int, prologue: bool) -> int:
+            if qtype == mm.TYPE_Q4_K and m <= 3:
+                return 2  # activation image (with the prologue) + row GEMV
+            groups = (m + 15) // 16 if qtype == mm.TYPE_Q4_K else (m + 7) // 8
+            return (1 if prologue else 0) + 2 * groups
+
         n = 0
-        for lw in self.layers:
-            n += 2  # rms norms
+        for il, lw in enumerate(self.layers):
             if lw.q is not None or lw.k is not None or lw.v is not None:
-                n += 2  # quantize + fused q/k/v gemv
-            n += 2 if lw.o is not None else 0
-            n += 1  # residual add
-            n += 2 + 1 + 2 + 1  # gate/up (quantize + gemv), swiglu, down (quantize + gemv), add
+                n += fused(mm.TYPE_Q4_K, True)
+            elif il > 0:
+                n += 1  # residual add
+            n += fused(mm.TYPE_Q4_K, False) if lw.o is not None else 0
+            n += fused(mm.TYPE_Q4_K, True) * 2  # gate/up, down
         if self.head is not None:
-            n += 1 + 2 + 1
+            n += fused(mm.TYPE_Q6_K, True) + 1
+        else:
+            n += 1
         return n
 
     # -- one step ----------------------------------------------------------
@@ -156,36 +167,53 @@ class Stack:
         return buf.view(-1)[: self.m * n].view(self.m, n)
 
     def step_body(self) -> None:
-        """Enqueue one decode/verify step on the current stream (h is updated in place)."""
-        for il, lw in enumerate(self.layers):
-            mm.rms_norm(self.h, None, self.eps, out=self.xn)
+        """Enqueue one decode/verify step on the current stream.
+
+        Four fused calls per layer: the residual add of the previous projection
+        and the RMS norm run in the quantizer of the next one (h ping-pongs
+        between two buffers), SwiGLU runs in the quantizer of ffn_down.
+        On return self.h holds the final residual stream."""
+        h, h_alt = self.h, self.h_alt
+        part_live = False  # self.part holds a projection output still to be added to h
+        for lw in self.layers:
+            # attention block: xn = rms(h [+ part]) -> q, k, v
             ws, outs = [], []
             for w, b in ((lw.q, self.qb), (lw.k, self.kb), (lw.v, self.vb)):
                 if w is not None:
                     ws.append(w)
                     outs.append(self._sl(b, w.n))
-            if ws:
-                mm.mul_mat_multi(ws, self.xn, outs)
+            if part_live:
+                if ws:
+                    mm.mul_mat_fused(ws, h, outs, mode=mm.PRO_RMS, r=self.part, h_out=h_alt, eps=self.eps)
+                    h, h_alt = h_alt, h
+                else:
+                    mm.add_(h, self.part)  # no attention rows on this rank: fold the residual in place
+            elif ws:
+                mm.mul_mat_fused(ws, h, outs, mode=mm.PRO_RMS, eps=self.eps)
+            # o projection (row-parallel)
             if lw.o is not None:
                 mm.mul_mat(lw.o, self._sl(self.qb, lw.o.k), out=self.part)
             else:
                 self.part.zero_()
             if self.world > 1:
                 self.comm.allreduce_(self.part)
-            mm.add_(self.h, self.part)
-            mm.rms_norm(self.h, None, self.eps, out=self.xn)
+            # ffn: xn = rms(h + part) -> gate, up ; h_alt = h + part
             nf = lw.gate.n
-            g, u, a = self._sl(self.gb, nf), self._sl(self.ub, nf), self._sl(self.act, nf)
-            mm.mul_mat_multi([lw.gate, lw.up], self.xn, [g, u])
-            mm.swiglu(g, u, out=a)
-            mm.mul_mat(lw.down, a, out=self.part)
+            g, u = self._sl(self.gb, nf), self._sl(self.ub, nf)
+            mm.mul_mat_fused([lw.gate, lw.up], h, [g, u], mode=mm.PRO_RMS, r=self.part, h_out=h_alt, eps=self.eps)
+            h, h_alt = h_alt, h
+            # down (row-parallel) with silu(gate) * up fused into its quantizer
+            mm.mul_mat_fused([lw.down], g, [self.part], mode=mm.PRO_SWIGLU, r=u)
             if self.world > 1:
                 self.comm.allreduce_(self.part)
-            mm.add_(self.h, self.part)
+            part_live = True
         if self.head is not None:
-            mm.rms_norm(self.h, None, self.eps, out=self.xn)
-            mm.mul_mat(self.head, self.xn, out=self.logits)
+            mm.mul_mat_fused([self.head], h, [self.logits], mode=mm.PRO_RMS, r=self.part, h_out=h_alt, eps=self.eps)
+            h, h_alt = h_alt, h
             mm.argmax(self.logits, out=self.tok)
+        elif part_live:
+            mm.add_(h, self.part)
+        self.h_final = h
 
     def capture(self) -> None:
         """Capture step_body() into a CUDA graph (run one eager step first to warm up)."""

@@ -99,6 +99,31 @@ cpq_status cpq_mul_mat_ws(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *
 cpq_status cpq_mul_mat_multi(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
                              void *stream);
 
+/* Fused prologue applied to X before it is quantized, mirroring the ops that
+ * precede the projections in codpiece's layer (qwen35.rs:2534-2537 rms(),
+ * 2777 residual add, 2781 silu*mul):
+ *   CPQ_PRO_NONE     X
+ *   CPQ_PRO_RMS      rms_norm(X + r) * g     r, g optional (NULL); when h_out is
+ *                                            non-NULL, X + r is also stored there
+ *                                            (the residual stream; must not alias X/r)
+ *   CPQ_PRO_SWIGLU   silu(X) * r             X = gate, r = up
+ * r and h_out have X's shape and row stride; g has K floats. */
+typedef enum { CPQ_PRO_NONE = 0, CPQ_PRO_RMS = 1, CPQ_PRO_SWIGLU = 2 } cpq_prologue_mode;
+
+typedef struct cpq_prologue {
+    int32_t mode;
+    const float *r;
+    const float *g;
+    float *h_out;
+    float eps;
+} cpq_prologue;
+
+/* cpq_mul_mat_multi with a fused prologue: Y_i = W_i x quantize(f(X)). The
+ * prologue runs once per call (inside the quantizer on the decode path), so a
+ * decode layer is four of these calls (q/k/v, o, gate/up, down). */
+cpq_status cpq_mul_mat_fused(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
+                             const cpq_prologue *pro, void *stream);
+
 /* Activation re-quantization as ggml-cpu's from_float for the vec_dot_type of
  * wtype (Q8_K for Q4_K/Q6_K, Q8_0 for Q8_0): m rows of k floats (row stride k)
  * into m*k/blck ggml blocks (block_q8_K 292 B, block_q8_0 34 B) at out. */

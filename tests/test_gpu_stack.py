@@ -34,7 +34,7 @@ def test_stack_matches_cpu_restatement(cuda, oracle, m):
     s.h.copy_(h0)
     s.step_body()
     torch.cuda.synchronize()
-    h_gpu = s.h.cpu().numpy()
+    h_gpu = s.h_final.cpu().numpy()
     logits_gpu = s.logits.cpu().numpy()
     tok_gpu = s.tok.cpu().numpy()
 
@@ -59,11 +59,11 @@ def test_graph_replay_equals_eager(cuda):
     s.h.copy_(h0)
     s.step_body()
     torch.cuda.synchronize()
-    eager = (s.h.clone(), s.logits.clone(), s.tok.clone())
+    eager = (s.h_final.clone(), s.logits.clone(), s.tok.clone())
     s.h.copy_(h0)
     s.capture()              # runs one eager step, then captures
     s.h.copy_(h0)
     s.replay()
     torch.cuda.synchronize()
-    assert torch.equal(s.h, eager[0]) and torch.equal(s.logits, eager[1]) and torch.equal(s.tok, eager[2])
+    assert torch.equal(s.h_final, eager[0]) and torch.equal(s.logits, eager[1]) and torch.equal(s.tok, eager[2])
     s.release()
