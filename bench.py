@@ -102,7 +102,7 @@ class ClockSampler:
 
 def traffic_from_profiles():
     """Per-launch DRAM bytes of the Q4_K GEMV from the committed ncu summary (or None)."""
-    p = ROOT / "profiles" / "gemv_q4k_ffn.md"
+    p = ROOT / "profiles" / "gemv_q4k_row_ffn.md"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -178,7 +178,7 @@ def kernel_roofline(torch, mm, stream, sets: int = 4, reps: int = 20):
     del g
     return {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
             "traffic": traffic, "peak_kind": kind,
-            "kernel": "Q4_K mul_mat M=1 (quantize_q8K + gemv_kernel<FmtQ4K,1>), config 2 shapes",
+            "kernel": "Q4_K mul_mat M=1 (act_prep_kernel + gemv_q4k_row_kernel<1>), config 2 shapes",
             "algorithmic_bytes_per_launch": int(algo), "avg_launch_us": round(per_op_s * 1e6, 3),
             "launches_timed": reps * len(ws)}
 
