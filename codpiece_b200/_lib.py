@@ -26,7 +26,7 @@ STATUS = {
 # Every symbol include/cpq.h declares (checked by tests/test_abi.py).
 EXPORTED = [
     "cpq_init", "cpq_release", "cpq_mul_mat_workspace_size", "cpq_mul_mat", "cpq_mul_mat_ws",
-    "cpq_mul_mat_multi", "cpq_mul_mat_fused", "cpq_quantize_act", "cpq_rms_norm", "cpq_swiglu", "cpq_add_inplace", "cpq_argmax",
+    "cpq_mul_mat_multi", "cpq_mul_mat_fused", "cpq_mul_mat_noalloc", "cpq_quantize_act", "cpq_rms_norm", "cpq_swiglu", "cpq_add_inplace", "cpq_argmax",
     "cpq_tp_split_state", "cpq_tp_unique_id", "cpq_tp_comm_init", "cpq_tp_allreduce_f32", "cpq_tp_comm_check",
     "cpq_tp_comm_destroy", "cpq_synth_weights", "cpq_device_status", "cpq_last_error", "cpq_status_string",
     "cpq_abi_version",
@@ -82,6 +82,7 @@ def lib() -> C.CDLL:
         "cpq_mul_mat_ws": (st, [P(CpqTensor), P(CpqTensor), P(CpqTensor), vp, sz, vp]),
         "cpq_mul_mat_multi": (st, [P(P(CpqTensor)), P(P(CpqTensor)), C.c_int, P(CpqTensor), vp]),
         "cpq_mul_mat_fused": (st, [P(P(CpqTensor)), P(P(CpqTensor)), C.c_int, P(CpqTensor), P(CpqPrologue), vp]),
+        "cpq_mul_mat_noalloc": (st, [P(CpqTensor), P(CpqTensor), P(CpqTensor), vp]),
         "cpq_quantize_act": (st, [i32, vp, vp, i64, i64, vp]),
         "cpq_rms_norm": (st, [vp, vp, vp, i64, i64, C.c_float, vp]),
         "cpq_swiglu": (st, [vp, vp, vp, i64, vp]),

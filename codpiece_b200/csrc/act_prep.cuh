@@ -27,7 +27,7 @@ namespace cpq {
 
 enum ActMode : int { kActPlain = 0, kActRms = 1, kActSwiglu = 2 };
 
-__host__ __device__ inline int row_act_bytes(int64_t k, int m) {
+__host__ __device__ constexpr int row_act_bytes(int64_t k, int m) {
     return int(align_up(align_up(size_t(m) * size_t(k), 16) + align_up(size_t(m) * size_t(k / kQK_K) * 4, 16) +
                             size_t(m) * size_t(k / kQK_K) * 16,
                         128));

@@ -186,7 +186,7 @@ struct ActLayout {
     size_t qs_off, d_off, bs_off, bytes;
 };
 
-__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+__host__ __device__ constexpr size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 inline ActLayout act_layout(int vec_type, int64_t k, int64_t m) {
     ActLayout l;

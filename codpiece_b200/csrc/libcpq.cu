@@ -13,6 +13,7 @@
 //   split.inl        tensor-parallel partition rules (host)
 //   tp.inl           NCCL communicator (host)
 //   api.inl          extern "C" entry points declared in include/cpq.h
+//   noalloc.inl      cpq_mul_mat_noalloc: decode GEMV on static device scratch
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ < 1000
 #error "libcpq targets sm_100a (B200) only"
 #endif
@@ -33,3 +34,4 @@
 #include "split.inl"
 #include "tp.inl"
 #include "api.inl"
+#include "noalloc.inl"

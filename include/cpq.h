@@ -124,6 +124,20 @@ typedef struct cpq_prologue {
 cpq_status cpq_mul_mat_fused(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
                              const cpq_prologue *pro, void *stream);
 
+/* No counterpart in the reference: an entry point for callers that cannot
+ * allocate device memory when they run the product (inside a CUDA graph
+ * capture, under a host engine that owns every device allocation, or on a
+ * thread that must not take the implicit device synchronization of
+ * cudaMalloc/cudaFree). Same result as cpq_mul_mat, but all scratch lives in
+ * one static device array of about 2.5 MB that the library reserves on every
+ * GPU that loads it, held until the process exits; no cudaMalloc, no
+ * cudaFree, no cpq_init needed. Limits: Q4_K weights only, M <= 3 tokens,
+ * K <= 32768, N <= 262144 rows; anything larger returns CPQ_ERR_UNSUPPORTED
+ * without launching. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress), so make it before any stream capture. All
+ * calls share the array: calls whose executions overlap on the GPU race. */
+cpq_status cpq_mul_mat_noalloc(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *y, void *stream);
+
 /* Activation re-quantization as ggml-cpu's from_float for the vec_dot_type of
  * wtype (Q8_K for Q4_K/Q6_K, Q8_0 for Q8_0): m rows of k floats (row stride k)
  * into m*k/blck ggml blocks (block_q8_K 292 B, block_q8_0 34 B) at out. */
