@@ -39,7 +39,10 @@ constexpr size_t kWsCounters = 65536;                       // row blocks per ca
 constexpr size_t kWsCountersBytes = kWsCounters * sizeof(int);
 constexpr size_t kWsMaxWarps = 148 * 2 * 16;                // persistent warps, generous
 constexpr size_t kWsPartialBytes = kWsMaxWarps * 2 * 16 * 16 * sizeof(float);
-constexpr size_t kWsActOffset = kWsCountersBytes + kWsPartialBytes;
+constexpr int kArgmaxChunks = 128;                            // CTAs per argmax row
+constexpr int kArgmaxMaxRows = 64;
+constexpr size_t kWsAuxBytes = align_up(size_t(kArgmaxMaxRows) * (kArgmaxChunks * 8 + 4), 256);
+constexpr size_t kWsActOffset = kWsCountersBytes + kWsPartialBytes + kWsAuxBytes;
 
 struct DevState {
     void *ws = nullptr;
@@ -736,7 +739,20 @@ cpq_status cpq_add_inplace(float *y, const float *x, int64_t n, void *stream) {
 cpq_status cpq_argmax(const float *x, int64_t n, int64_t m, int32_t *out, void *stream) {
     if (!x || !out || n <= 0 || m < 0 || n > 2147483647) return fail(CPQ_ERR_INVALID_ARG, "argmax arguments");
     if (m == 0) return CPQ_SUCCESS;
-    cudaError_t e = launch(argmax_kernel, dim3(unsigned(m)), dim3(1024), 0, static_cast<cudaStream_t>(stream), x, n, out);
+    if (m > kArgmaxMaxRows) return fail(CPQ_ERR_UNSUPPORTED, "argmax: at most %d rows per call", kArgmaxMaxRows);
+    void *ws;
+    size_t bytes;
+    cpq_status rc = workspace_of_current(&ws, &bytes);
+    if (rc) return rc;
+    // aux area after the row-block counters and partials: [rows][chunks] values, indices, then row counters
+    uint8_t *aux = static_cast<uint8_t *>(ws) + kWsCountersBytes + kWsPartialBytes;
+    float *pval = reinterpret_cast<float *>(aux);
+    int32_t *pidx = reinterpret_cast<int32_t *>(aux + size_t(kArgmaxMaxRows) * kArgmaxChunks * 4);
+    int *cnt = reinterpret_cast<int *>(aux + size_t(kArgmaxMaxRows) * kArgmaxChunks * 8);
+    const int64_t nchunk = std::min<int64_t>(kArgmaxChunks, (n + 2047) / 2048);
+    const int64_t chunk = (n + nchunk - 1) / nchunk;
+    cudaError_t e = launch(argmax_kernel, dim3(unsigned(nchunk), unsigned(m)), dim3(256), 0,
+                           static_cast<cudaStream_t>(stream), x, n, chunk, pval, pidx, cnt, out);
     return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "argmax launch");
 }
 

@@ -100,45 +100,56 @@ __global__ void add_inplace_kernel(float *__restrict__ y, const float *__restric
         y[i] = __fadd_rn(y[i], x[i]);
 }
 
-// First index of the maximum of each row (NaN-free input assumed).
-__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ x, int64_t n,
-                                                     int32_t *__restrict__ out) {
+// First index of the maximum of each row (NaN-free input assumed). Grid
+// (nchunk, m): each CTA reduces one chunk of a row to (max, first index),
+// publishes it, and the last CTA of the row (counter, acq_rel) reduces the
+// chunk results in chunk order and resets the counter for the next call.
+__device__ __forceinline__ void argmax_merge(float &best, int32_t &bi, float ov, int32_t oi) {
+    if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+    }
+}
+
+__global__ void __launch_bounds__(256) argmax_kernel(const float *__restrict__ x, int64_t n, int64_t chunk,
+                                                    float *__restrict__ pval, int32_t *__restrict__ pidx,
+                                                    int *__restrict__ counters, int32_t *__restrict__ out) {
     pdl_wait();
     pdl_launch_dependents();
-    __shared__ float sv[32];
-    __shared__ int32_t si[32];
-    const float *xr = x + int64_t(blockIdx.x) * n;
+    __shared__ float sv[8];
+    __shared__ int32_t si[8];
+    __shared__ int last;
+    const int64_t row = blockIdx.y;
+    const int nchunk = gridDim.x;
+    const float *xr = x + row * n;
+    const int64_t lo = int64_t(blockIdx.x) * chunk, hi = min(n, lo + chunk);
     float best = -INFINITY;
     int32_t bi = 0x7fffffff;
-    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = xr[i];
-        if (v > best) {
-            best = v;
-            bi = int32_t(i);
-        }
-    }
+    for (int64_t i = lo + threadIdx.x; i < hi; i += 256) argmax_merge(best, bi, xr[i], int32_t(i));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > best || (ov == best && oi < bi)) {
-            best = ov;
-            bi = oi;
-        }
-    }
-    const int w = threadIdx.x >> 5;
+    for (int o = 16; o > 0; o >>= 1)
+        argmax_merge(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
     if ((threadIdx.x & 31) == 0) {
-        sv[w] = best;
-        si[w] = bi;
+        sv[threadIdx.x >> 5] = best;
+        si[threadIdx.x >> 5] = bi;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int q = 1; q < int(blockDim.x >> 5); q++)
-            if (sv[q] > best || (sv[q] == best && si[q] < bi)) {
-                best = sv[q];
-                bi = si[q];
-            }
-        out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+        for (int w = 1; w < 8; w++) argmax_merge(best, bi, sv[w], si[w]);
+        pval[row * nchunk + blockIdx.x] = best;
+        pidx[row * nchunk + blockIdx.x] = bi;
+        int old;
+        asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(counters + row) : "memory");
+        last = (old == nchunk - 1);
+    }
+    __syncthreads();
+    if (!last) return;
+    if (threadIdx.x == 0) {
+        float b = -INFINITY;
+        int32_t ix = 0x7fffffff;
+        for (int c = 0; c < nchunk; c++) argmax_merge(b, ix, __ldcg(pval + row * nchunk + c), __ldcg(pidx + row * nchunk + c));
+        out[row] = ix == 0x7fffffff ? 0 : ix;
+        counters[row] = 0;
     }
 }
 

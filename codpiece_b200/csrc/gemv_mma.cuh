@@ -378,14 +378,14 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __gr
                     for (int p = 0; p < npieces; p++) {
                         const int64_t gp = first + p;
                         const int sl = (c_mb == (gp * T / G) / nbk) ? 0 : 1;
-                        const volatile float *q = a.partials + (size_t(gp) * 2 + sl) * (kMmaRows * kMmaMaxTokens);
+                        const float *q = a.partials + (size_t(gp) * 2 + sl) * (kMmaRows * kMmaMaxTokens);
 #pragma unroll
                         for (int ng = 0; ng < NG; ng++)
 #pragma unroll
                             for (int i = 0; i < 4; i++) {
                                 const int t = ng * 8 + 2 * tig + (i & 1);
                                 const int r = gid + 8 * (i >> 1);
-                                sum[ng][i] += q[r * kMmaMaxTokens + t];
+                                sum[ng][i] += __ldcg(q + r * kMmaMaxTokens + t);
                             }
                     }
 #pragma unroll

@@ -220,9 +220,9 @@ __global__ void __launch_bounds__(kRowWarps * 32, 1) gemv_q4k_row_kernel(const _
                     for (int p = 0; p < npieces; p++) {
                         const int64_t gp = first + p;
                         const int sl = (c_mb == (gp * T / G) / nbk) ? 0 : 1;
-                        const volatile float *q = a.partials + (size_t(gp) * 2 + sl) * 256;
+                        const float *q = a.partials + (size_t(gp) * 2 + sl) * 256;
 #pragma unroll
-                        for (int t = 0; t < MT; t++) sum[t] += q[lane * 4 + t];
+                        for (int t = 0; t < MT; t++) sum[t] += __ldcg(q + lane * 4 + t);
                     }
 #pragma unroll
                     for (int t = 0; t < MT; t++)
