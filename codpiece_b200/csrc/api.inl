@@ -354,6 +354,38 @@ static cpq_status q4k_tensor_map(const uint8_t *w, int64_t n, int64_t k, size_t 
     return CPQ_SUCCESS;
 }
 
+// Dense fp16 activations [m][k] as a 2-D tensor for the tensor-core GEMM:
+// box = 64 elements (128 bytes) x tile_n rows, 128-byte swizzle.
+static cpq_status f16_act_tensor_map(const __half *x, int64_t k, int64_t m, int tile_n, CUtensorMap *out) {
+    static std::mutex mu;
+    static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> cache;
+    const TmapKey key{x, m, k, size_t(k) * 2, tile_n, 0};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *out = it->second;
+            return CPQ_SUCCESS;
+        }
+    }
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return fail(CPQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(m)};
+    const cuuint64_t strides[1] = {cuuint64_t(k) * 2};
+    const cuuint32_t box[2] = {cuuint32_t(kTcK), cuuint32_t(tile_n)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUtensorMap t;
+    const CUresult r = enc(&t, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(x), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(CPQ_ERR_CUDA, "cuTensorMapEncodeTiled (fp16 activations) failed (%d)", int(r));
+    std::lock_guard<std::mutex> lk(mu);
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, t);
+    *out = t;
+    return CPQ_SUCCESS;
+}
+
 // Activation region bytes (the largest of the three layouts) and the fp32
 // prologue region that follows it.
 static size_t act_region_bytes(int32_t vt, int64_t k, int64_t m);
@@ -444,6 +476,7 @@ static size_t act_region_bytes(int32_t vt, int64_t k, int64_t m) {
     if (vt == CPQ_TYPE_Q8_K) {
         b = std::max(b, frag_bytes(k, 16));
         b = std::max(b, size_t(row_act_bytes(k, kRowMaxTokens)));
+        b = std::max(b, size_t(m) * size_t(k) * 2);  // fp16 activations of the tensor-core path
     }
     return align_up(b, 256);
 }
@@ -492,6 +525,51 @@ static cpq_status run_q4k_mma(const GemvArgs &g, const float *x, int64_t x_strid
         for (int i = 0; i < g.n_w; i++) a.y[i] = g.y[i] + t0 * g.y_stride[i];
         e = mt <= 8 ? launch_q4k_mma_t<1>(a, st) : launch_q4k_mma_t<2>(a, st);
         if (e != cudaSuccess) return cuda_fail(e, "q4_K gemv launch");
+    }
+    return CPQ_SUCCESS;
+}
+
+// M > 16 (chunked prefill): X is Q8_K-quantized once into fp16 d*q, then each
+// weight runs as one tcgen05 GEMM launch (gemm_tc.cuh). Token tiles are as
+// few as possible and balanced (tile_n a multiple of 16, at most 256).
+static cpq_status run_q4k_tc(const GemvArgs &g, const float *x, int64_t x_stride, int64_t m, uint8_t *ws,
+                             cudaStream_t st) {
+    const int64_t k = g.k, nbk = k / kQK_K;
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return fail(CPQ_ERR_CUDA, "no current device");
+    static std::atomic<int> set[kMaxDevices];
+    if (!set[dev].load(std::memory_order_relaxed)) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(gemm_q4k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+        if (e != cudaSuccess) return cuda_fail(e, "tensor-core gemm smem attribute");
+        set[dev].store(1, std::memory_order_relaxed);
+    }
+    const int64_t n_tok_tiles = (m + kTcMaxTok - 1) / kTcMaxTok;
+    const int tile_n = int(align_up(size_t((m + n_tok_tiles - 1) / n_tok_tiles), 16));
+    __half *xh = reinterpret_cast<__half *>(ws + kWsActOffset);
+
+    const int64_t qwarps = m * nbk;
+    cudaError_t e = launch(act_f16_kernel, dim3(unsigned(std::min<int64_t>((qwarps + 7) / 8, 148 * 64))), dim3(256),
+                           0, st, x, k, m, x_stride, xh);
+    if (e != cudaSuccess) return cuda_fail(e, "fp16 activation launch");
+
+    static thread_local TcArgs a;
+    std::memset(&a, 0, sizeof a);
+    cpq_status rc = f16_act_tensor_map(xh, k, m, tile_n, &a.tmap_x);
+    if (rc) return rc;
+    a.m = m;
+    a.nbk = int(nbk);
+    a.tile_n = tile_n;
+    for (int i = 0; i < g.n_w; i++) {
+        const int64_t n = g.row_start[i + 1] - g.row_start[i];
+        if (n == 0) continue;
+        if ((rc = q4k_tensor_map(g.w[i], n, k, g.rs, &a.tmap_w, kTcRows, 1))) return rc;
+        a.y = g.y[i];
+        a.y_stride = g.y_stride[i];
+        a.n = n;
+        const dim3 grid(unsigned(n_tok_tiles), unsigned((n + kTcRows - 1) / kTcRows));
+        e = launch(gemm_q4k_tc_kernel, grid, dim3(kTcThreads), size_t(kTcSmem), st, a);
+        if (e != cudaSuccess) return cuda_fail(e, "tensor-core gemm launch");
     }
     return CPQ_SUCCESS;
 }
@@ -554,7 +632,8 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
         xp = tmp;
         x_stride = s0.k;
     }
-    if (s0.wtype == CPQ_TYPE_Q4_K) return run_q4k_mma(a, xp, x_stride, m, wsb, st);
+    if (s0.wtype == CPQ_TYPE_Q4_K)
+        return m > kMmaMaxTokens ? run_q4k_tc(a, xp, x_stride, m, wsb, st) : run_q4k_mma(a, xp, x_stride, m, wsb, st);
 
     void *act_ws = wsb + kWsActOffset;
     e = launch_quantize(vt, xp, s0.k, m, x_stride, act_ws, L, nullptr, st);

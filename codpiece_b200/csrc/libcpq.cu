@@ -8,6 +8,7 @@
 //   gemv_mma.cuh     Q4_K verify GEMM (M 4..16) on int8 mma tiles, stream-K
 //   act_prep.cuh     decode activation image: fused rms/swiglu prologue + Q8_K
 //   gemv_row.cuh     Q4_K decode GEMV (M 1..3), lane per row
+//   gemm_tc.cuh      Q4_K chunked-prefill GEMM (M > 16) on tcgen05 tensor cores
 //   elementwise.cuh  rms norm, SwiGLU, residual add, argmax
 //   synth.cuh        seeded synthetic weights
 //   split.inl        tensor-parallel partition rules (host)
@@ -29,6 +30,7 @@
 #include "gemv_mma.cuh"
 #include "act_prep.cuh"
 #include "gemv_row.cuh"
+#include "gemm_tc.cuh"
 #include "quantize.cuh"
 #include "synth.cuh"
 #include "split.inl"
