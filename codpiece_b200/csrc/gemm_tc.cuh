@@ -10,22 +10,32 @@
 // and X~ as fp16(d_x*q_x). At the benchmark's value distributions that is a
 // max |dy| / max |y| of about 4e-4 (the parity bound is 1e-3).
 //
+// K order. Both operands store K permuted inside every group of 8 elements
+// as (0,2,1,3,4,6,5,7): a 32-bit word of Q4_K nibbles then yields two fp16
+// pairs with one mask each (bits 0-3|16-19 and, shifted by 8, 8-11|24-27).
+// The dot product is unchanged because A and B use the same order.
+//
 // One CTA computes a 128-row x tile_n-token tile of Y (tile_n a multiple of
-// 16, at most 256) over the whole K, in stages of 64 K elements (one 128-byte
-// swizzle atom per row):
-//   warp 0      one lane issues tcgen05.mma.cta_group::1.kind::f16, 4 x K=16
-//               per stage, into a tile_n-column fp32 TMEM accumulator, and
-//               commits each stage back to its "empty" barrier
+// 16, at most 256) over the whole K, in stages of 64 K elements. The
+// dequantized weights (operand A) never touch shared memory: they are
+// written to tensor memory with tcgen05.st and the MMA reads A from there,
+// which leaves shared-memory bandwidth to the activation operand (B).
+// TMEM: 512 columns = the fp32 accumulator (columns 0-255, lane = tile row,
+// column = token) + kTcAStages A stages of 32 columns (64 fp16 per lane).
+//   warp 0      one lane issues tcgen05.mma.cta_group::1.kind::f16 with A in
+//               TMEM and B in shared memory, 4 x K=16 per stage, and commits
+//               each stage back to the "emptyA"/"emptyB" barriers
 //   warp 1      one lane TMA-loads the activation stage (box 64 x tile_n fp16,
-//               SWIZZLE_128B, no multicast) onto "fullB"
+//               SWIZZLE_128B K-major, no multicast) onto "fullB"
 //   warp 2      one lane TMA-loads the tile's raw Q4_K superblocks (box 128
-//               rows x 144 bytes) into a 3-slot ring ("rawFull"/"rawEmpty")
-//   warps 4-7   thread r dequantizes tile row r from the raw ring into the
-//               SWIZZLE_128B K-major A stage (the layout the UMMA descriptor
-//               names), fences the async proxy, and the warp arrives on
-//               "fullA"; after the K loop the same warps read the accumulator
-//               (tcgen05.ld 32x32b: warp w sees TMEM lanes 32*(w%4)..+31 =
-//               tile rows) and store Y, 32 tokens at a time.
+//               rows x 144 bytes) into the raw ring ("rawFull"/"rawEmpty")
+//   warps 4-11  dequantize: warp w owns TMEM lanes (tile rows) 32*(w%4)..+31,
+//               warps 4-7 the even stages, 8-11 the odd ones; a thread turns
+//               its row's 32 bytes of nibbles into 64 fp16 and stores them as
+//               32 columns with tcgen05.st; the warp arrives on "fullA".
+//               After the K loop they read the accumulator (tcgen05.ld
+//               32x32b), warps 4-7 the first half of the token columns, 8-11
+//               the second, and store Y.
 // Waits are bounded (kWaitLimitNs); a timeout sets g_dev_error and a CTA-wide
 // abort flag, every role skips to the end, the TMA lanes wait (bounded) for
 // their copies in flight, the MMA lane for its last commit, and warp 0 frees
@@ -43,16 +53,30 @@ namespace cpq {
 constexpr int kTcRows = 128;      // weight rows per tile (MMA M)
 constexpr int kTcMaxTok = 256;    // tokens per tile at most (MMA N)
 constexpr int kTcK = 64;          // K elements per stage
-constexpr int kTcStages = 3;      // A/B stage ring
-constexpr int kTcRawSlots = 3;    // raw superblock ring
-constexpr int kTcThreads = 256;
-constexpr int kTcABytes = kTcRows * 128;
+#ifndef CPQ_TC_A_STAGES
+#define CPQ_TC_A_STAGES 4
+#endif
+#ifndef CPQ_TC_B_STAGES
+#define CPQ_TC_B_STAGES 4
+#endif
+#ifndef CPQ_TC_RAW_SLOTS
+#define CPQ_TC_RAW_SLOTS 3
+#endif
+constexpr int kTcAStages = CPQ_TC_A_STAGES;    // dequantized weight stages in TMEM (32 columns each)
+constexpr int kTcBStages = CPQ_TC_B_STAGES;    // activation stages in shared memory (32 KB each)
+constexpr int kTcRawSlots = CPQ_TC_RAW_SLOTS;  // raw superblock slots in shared memory (18 KB each)
+constexpr uint32_t kTcAccCols = 256;           // accumulator columns (tile_n <= 256)
+constexpr uint32_t kTcTmemCols = 512;
+static_assert(kTcAccCols + 32 * kTcAStages <= kTcTmemCols, "TMEM columns");
+constexpr int kTcThreads = 384;  // 4 role warps + 8 dequantizing warps
+constexpr int kTcDqWarps = 8;
 constexpr int kTcBBytes = kTcMaxTok * 128;
 constexpr int kTcRawBytes = kTcRows * kQ4K_Bytes;
-constexpr int kTcBarOffset = kTcStages * (kTcABytes + kTcBBytes) + kTcRawSlots * kTcRawBytes;
+constexpr int kTcBarOffset = kTcBStages * kTcBBytes + kTcRawSlots * kTcRawBytes;
 constexpr int kTcSmem = kTcBarOffset + 256 /* barriers, TMEM slot, abort flag */ + 1024 /* alignment slack */;
-static_assert(kTcRawBytes % 1024 == 0 && kTcABytes % 1024 == 0 && kTcBBytes % 1024 == 0, "1024-byte stage bases");
+static_assert(kTcRawBytes % 1024 == 0 && kTcBBytes % 1024 == 0, "1024-byte stage bases");
 static_assert(kTcSmem <= 227 * 1024, "shared memory");
+static_assert((2 * (kTcAStages + kTcBStages + kTcRawSlots) + 1) * 8 + 8 <= 256, "barrier area");
 
 struct alignas(64) TcArgs {
     CUtensorMap tmap_x;  // fp16 activations [m][k], box 64 x tile_n, SWIZZLE_128B
@@ -64,11 +88,6 @@ struct alignas(64) TcArgs {
     int nbk;             // superblocks per row
     int tile_n;          // tokens per tile (multiple of 16, 16..256)
 };
-
-// TMEM columns for a tile_n-column accumulator: a power of two, at least 32.
-__host__ __device__ constexpr uint32_t tc_tmem_cols(int tile_n) {
-    return tile_n <= 32 ? 32u : tile_n <= 64 ? 64u : tile_n <= 128 ? 128u : 256u;
-}
 
 // ---- tcgen05 / descriptor helpers ------------------------------------------
 
@@ -88,13 +107,15 @@ __host__ __device__ constexpr uint32_t tc_idesc_f16(int m, int n) {
     return (1u << 4) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
-__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate) {
+// D (TMEM) (+)= A (TMEM, K-major: lane = row, two 16-bit K elements per
+// 32-bit column) x B (shared-memory descriptor).
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -136,6 +157,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%"
+        "18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Bounded wait that also gives up as soon as another role of the CTA aborted.
 __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -170,12 +204,12 @@ __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<co
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid_constant__ TcArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sA = smem;
-    uint8_t *sB = sA + kTcStages * kTcABytes;
-    uint8_t *sRaw = sB + kTcStages * kTcBBytes;
+    uint8_t *sB = smem;
+    uint8_t *sRaw = sB + kTcBStages * kTcBBytes;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kTcBarOffset);
-    uint64_t *fullA = bars, *fullB = bars + kTcStages, *empty = bars + 2 * kTcStages;
-    uint64_t *rawFull = bars + 3 * kTcStages, *rawEmpty = rawFull + kTcRawSlots, *done = rawEmpty + kTcRawSlots;
+    uint64_t *fullA = bars, *emptyA = fullA + kTcAStages;
+    uint64_t *fullB = emptyA + kTcAStages, *emptyB = fullB + kTcBStages;
+    uint64_t *rawFull = emptyB + kTcBStages, *rawEmpty = rawFull + kTcRawSlots, *done = rawEmpty + kTcRawSlots;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -184,17 +218,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
     const int64_t tok0 = int64_t(blockIdx.x) * tile_n;
     const int64_t row0 = int64_t(blockIdx.y) * kTcRows;
     const int nk = a.nbk * 4;
-    const uint32_t ncols = tc_tmem_cols(tile_n);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kTcStages; s++) {
-            mbar_init(&fullA[s], 4);  // one arrival per dequantizing warp
+        for (int s = 0; s < kTcAStages; s++) {
+            mbar_init(&fullA[s], kTcDqWarps / 2);  // the 4 warps that dequantize stage s
+            mbar_init(&emptyA[s], 1);
+        }
+        for (int s = 0; s < kTcBStages; s++) {
             mbar_init(&fullB[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&emptyB[s], 1);
         }
         for (int s = 0; s < kTcRawSlots; s++) {
             mbar_init(&rawFull[s], 1);
-            mbar_init(&rawEmpty[s], 4);
+            mbar_init(&rawEmpty[s], kTcDqWarps);
         }
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -202,14 +238,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
-                     "r"(ncols)
+                     "r"(kTcTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem = *tmem_slot;  // lane 0, column base: accumulator at +0, A stages at +kTcAccCols
 
     pdl_wait();  // weights, activations and Y may all belong to earlier kernels on the stream
     pdl_launch_dependents();
@@ -219,16 +255,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
         if (lane == 0) {
             const uint32_t idesc = tc_idesc_f16(kTcRows, tile_n);
             for (int t = 0; t < nk; t++) {
-                const int s = t % kTcStages;
-                const uint32_t ph = uint32_t(t / kTcStages) & 1u;
-                if (!tc_wait(&fullA[s], ph, abort_flag) || !tc_wait(&fullB[s], ph, abort_flag)) break;
+                const int sa = t % kTcAStages, sb = t % kTcBStages;
+                if (!tc_wait(&fullA[sa], uint32_t(t / kTcAStages) & 1u, abort_flag) ||
+                    !tc_wait(&fullB[sb], uint32_t(t / kTcBStages) & 1u, abort_flag))
+                    break;
                 tc_fence_after();
-                const uint64_t ad = smem_desc_sw128(smem_addr(sA + s * kTcABytes));
-                const uint64_t bd = smem_desc_sw128(smem_addr(sB + s * kTcBBytes));
+                const uint32_t at = tmem + kTcAccCols + 32u * uint32_t(sa);
+                const uint64_t bd = smem_desc_sw128(smem_addr(sB + sb * kTcBBytes));
 #pragma unroll
-                for (int kk = 0; kk < kTcK / 16; kk++)  // K=16 per MMA = 32 bytes = +2 in the start-address field
-                    tc_mma_f16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (t | kk) != 0 ? 1u : 0u);
-                tc_commit(&empty[s]);
+                for (int kk = 0; kk < kTcK / 16; kk++)  // K=16 per MMA: 8 TMEM columns of A, 32 bytes of B (+2)
+                    tc_mma_f16_ts(tmem, at + 8u * uint32_t(kk), bd + 2 * kk, idesc, (t | kk) != 0 ? 1u : 0u);
+                tc_commit(&emptyA[sa]);
+                tc_commit(&emptyB[sb]);
             }
             tc_commit(done);
             mbar_wait_bounded(done, 0);  // the accumulator is final (or idle) before TMEM is released
@@ -237,52 +275,48 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
     } else if (warp == 1) {
         // ---- activation stages (TMA) ----
         if (lane == 0) {
-            int last[kTcStages];
-#pragma unroll
-            for (int s = 0; s < kTcStages; s++) last[s] = -1;
-            for (int t = 0; t < nk; t++) {
-                const int s = t % kTcStages;
-                const uint32_t ph = uint32_t(t / kTcStages) & 1u;
-                if (!tc_wait(&empty[s], ph ^ 1u, abort_flag)) break;
+            int t = 0;
+            for (; t < nk; t++) {
+                const int s = t % kTcBStages;
+                const uint32_t ph = uint32_t(t / kTcBStages) & 1u;
+                if (!tc_wait(&emptyB[s], ph ^ 1u, abort_flag)) break;
                 mbar_arrive_expect_tx(&fullB[s], uint32_t(tile_n) * 128u);
                 tma_load_2d(sB + s * kTcBBytes, &a.tmap_x, t * kTcK, int(tok0), &fullB[s]);
-                last[s] = t;
             }
-#pragma unroll
-            for (int s = 0; s < kTcStages; s++)  // no copy may land after the CTA has exited
-                if (last[s] >= 0) mbar_wait_bounded(&fullB[s], uint32_t(last[s] / kTcStages) & 1u);
+            // no copy may land after the CTA has exited: wait for the last ones issued
+            for (int u = t > kTcBStages ? t - kTcBStages : 0; u < t; u++)
+                mbar_wait_bounded(&fullB[u % kTcBStages], uint32_t(u / kTcBStages) & 1u);
         }
         __syncwarp();
     } else if (warp == 2) {
         // ---- raw Q4_K superblocks (TMA) ----
         if (lane == 0) {
-            int last[kTcRawSlots];
-#pragma unroll
-            for (int s = 0; s < kTcRawSlots; s++) last[s] = -1;
-            for (int kb = 0; kb < a.nbk; kb++) {
+            int kb = 0;
+            for (; kb < a.nbk; kb++) {
                 const int s = kb % kTcRawSlots;
                 const uint32_t ph = uint32_t(kb / kTcRawSlots) & 1u;
                 if (!tc_wait(&rawEmpty[s], ph ^ 1u, abort_flag)) break;
                 mbar_arrive_expect_tx(&rawFull[s], uint32_t(kTcRawBytes));
                 tma_load_2d(sRaw + s * kTcRawBytes, &a.tmap_w, kb * (kQ4K_Bytes / 8), int(row0), &rawFull[s]);
-                last[s] = kb;
             }
-#pragma unroll
-            for (int s = 0; s < kTcRawSlots; s++)
-                if (last[s] >= 0) mbar_wait_bounded(&rawFull[s], uint32_t(last[s] / kTcRawSlots) & 1u);
+            for (int u = kb > kTcRawSlots ? kb - kTcRawSlots : 0; u < kb; u++)
+                mbar_wait_bounded(&rawFull[u % kTcRawSlots], uint32_t(u / kTcRawSlots) & 1u);
         }
         __syncwarp();
     } else if (warp >= 4) {
-        // ---- dequantization: thread r owns tile row r (rows past n arrive zero-filled) ----
-        const int r = threadIdx.x - 128;
-        const int sw = r & 7;  // the row's 16-byte chunk permutation in the swizzle atom
+        // ---- dequantization (rows past n arrive zero-filled, so they dequantize to 0) ----
+        const int dq = warp - 4;
+        const int grp = dq >> 2;                      // this warp's stages: t % 2 == grp
+        const int quarter = warp & 3;                 // TMEM lane quarter this warp may access
+        const int r = 32 * quarter + lane;            // tile row = TMEM lane
+        const uint32_t lane_base = uint32_t(32 * quarter) << 16;
         bool ok = true;
-        for (int t = 0; t < nk; t++) {
-            const int s = t % kTcStages;
-            const uint32_t ph = uint32_t(t / kTcStages) & 1u;
+        for (int t = grp; t < nk; t += 2) {
+            const int sa = t % kTcAStages;
+            const uint32_t pa = uint32_t(t / kTcAStages) & 1u;
             const int kb = t >> 2, j = t & 3;
             const int rs = kb % kTcRawSlots;
-            if (j == 0) {
+            if (j == grp) {  // this group's first stage of the superblock
                 ok = __all_sync(0xffffffffu, tc_wait(&rawFull[rs], uint32_t(kb / kTcRawSlots) & 1u, abort_flag));
                 if (!ok) break;
             }
@@ -290,7 +324,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
             const uint4 hd = *reinterpret_cast<const uint4 *>(raw);
             const uint4 qa = *reinterpret_cast<const uint4 *>(raw + 16 + 32 * j);
             const uint4 qb = *reinterpret_cast<const uint4 *>(raw + 32 + 32 * j);
-            if (j == 3) {  // last read of this superblock: hand the slot back
+            if (j == 2 + grp) {  // this group's last read of the superblock: hand the slot back
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&rawEmpty[rs]);
             }
@@ -304,44 +338,42 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
             const __half2 shi = __float2half2_rn(d * float((scw >> (sh + 8)) & 0xffu));
             const __half2 mlo = __float2half2_rn(-(dmin * float((mnw >> sh) & 0xffu)));
             const __half2 mhi = __float2half2_rn(-(dmin * float((mnw >> (sh + 8)) & 0xffu)));
-
-            ok = __all_sync(0xffffffffu, tc_wait(&empty[s], ph ^ 1u, abort_flag));
-            if (!ok) break;
-            uint8_t *arow = sA + s * kTcABytes + r * 128;
             const uint32_t wq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-            // byte i of the 32 holds element i (low nibble) and element 32+i (high nibble) of the stage
+            // word i holds elements 4i..4i+3 of sub-block 2j (low nibbles) and of 2j+1
+            // (high nibbles). Stage columns 0-15 are sub-block 2j, 16-31 sub-block 2j+1;
+            // word 2c+h fills columns 4c+2h (its elements 0, 2) and 4c+2h+1 (1, 3)
+            uint32_t v[32];
 #pragma unroll
             for (int c = 0; c < 4; c++) {
-                uint32_t lo[4], hi[4];
 #pragma unroll
-                for (int cc = 0; cc < 2; cc++) {
-                    const uint32_t w = wq[2 * c + cc];
-                    const uint32_t x01 = __byte_perm(w, 0, 0x4140);  // byte0 | byte1 << 16
-                    const uint32_t x23 = __byte_perm(w, 0, 0x4342);  // byte2 | byte3 << 16
-                    lo[2 * cc] = h2u(__hfma2(nib2h(x01), slo, mlo));
-                    lo[2 * cc + 1] = h2u(__hfma2(nib2h(x23), slo, mlo));
-                    hi[2 * cc] = h2u(__hfma2(nib2h(x01 >> 4), shi, mhi));
-                    hi[2 * cc + 1] = h2u(__hfma2(nib2h(x23 >> 4), shi, mhi));
+                for (int h = 0; h < 2; h++) {
+                    const uint32_t w = wq[2 * c + h];
+                    v[4 * c + 2 * h] = h2u(__hfma2(nib2h(w), slo, mlo));
+                    v[4 * c + 2 * h + 1] = h2u(__hfma2(nib2h(w >> 8), slo, mlo));
+                    v[16 + 4 * c + 2 * h] = h2u(__hfma2(nib2h(w >> 4), shi, mhi));
+                    v[16 + 4 * c + 2 * h + 1] = h2u(__hfma2(nib2h(w >> 12), shi, mhi));
                 }
-                // elements 8c..8c+7 are 16-byte chunk c, 32+8c.. chunk 4+c; chunk q sits at q ^ (row & 7)
-                *reinterpret_cast<uint4 *>(arow + ((c ^ sw) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                *reinterpret_cast<uint4 *>(arow + (((4 + c) ^ sw) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
             }
-            fence_proxy_async_smem();  // make the generic stores visible to the tensor core's async proxy
+            ok = __all_sync(0xffffffffu, tc_wait(&emptyA[sa], pa ^ 1u, abort_flag));
+            if (!ok) break;
+            tc_fence_after();  // the MMAs that read this A stage have completed
+            tmem_st32(tmem + lane_base + kTcAccCols + 32u * uint32_t(sa), v);
+            tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&fullA[s]);
+            if (lane == 0) mbar_arrive(&fullA[sa]);
         }
 
         // ---- epilogue: TMEM lane = tile row, column = token ----
         if (ok) ok = __all_sync(0xffffffffu, tc_wait(done, 0, abort_flag));
         if (ok) {
             tc_fence_after();
-            const int q = warp & 3;
-            const int64_t orow = row0 + 32 * q + lane;
+            const int64_t orow = row0 + r;
             const int64_t tend = a.m < tok0 + tile_n ? a.m : tok0 + tile_n;
-            for (int c0 = 0; c0 < tile_n && tok0 + c0 < tend; c0 += 32) {
+            const int half = (((tile_n + 1) / 2) + 31) & ~31;
+            const int cbeg = grp * half, cend = grp ? tile_n : (half < tile_n ? half : tile_n);
+            for (int c0 = cbeg; c0 < cend && tok0 + c0 < tend; c0 += 32) {
                 float v[32];
-                tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(c0), v);
+                tmem_ld32(tmem + lane_base + uint32_t(c0), v);
                 if (orow < a.n) {
                     float *yp = a.y + (tok0 + c0) * a.y_stride + orow;
 #pragma unroll
@@ -356,13 +388,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
     }
 }
 
 // The tensor-core path's activations: each 256-block of x quantized to Q8_K
 // exactly as quantize_row_q8_K does (q8k_quantize_block), then stored as
-// fp16(d*q), dense [m][k]. One warp per (token, block), grid-stride.
+// fp16(d*q), [m][k] with K permuted as (0,2,1,3,4,6,5,7) inside every group
+// of 8 (the A operand's order). One warp per (token, block), grid-stride.
 __global__ void __launch_bounds__(256) act_f16_kernel(const float *__restrict__ x, int64_t k, int64_t m,
                                                       int64_t x_stride, __half *__restrict__ out) {
     pdl_wait();
@@ -379,10 +412,11 @@ __global__ void __launch_bounds__(256) act_f16_kernel(const float *__restrict__ 
         const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
         int q[8];
         const float d = q8k_quantize_block(v, lane, q);
-        uint32_t h[4];
+        float f[8];
 #pragma unroll
-        for (int e = 0; e < 4; e++)
-            h[e] = h2u(__floats2half2_rn(__fmul_rn(d, float(q[2 * e])), __fmul_rn(d, float(q[2 * e + 1]))));
+        for (int e = 0; e < 8; e++) f[e] = __fmul_rn(d, float(q[e]));
+        const uint32_t h[4] = {h2u(__floats2half2_rn(f[0], f[2])), h2u(__floats2half2_rn(f[1], f[3])),
+                               h2u(__floats2half2_rn(f[4], f[6])), h2u(__floats2half2_rn(f[5], f[7]))};
         *reinterpret_cast<uint4 *>(out + row * k + b * kQK_K + lane * 8) = make_uint4(h[0], h[1], h[2], h[3]);
     }
 }
