@@ -372,7 +372,7 @@ static cpq_status f16_act_tensor_map(const __half *x, int64_t k, int64_t m, int 
     if (!enc) return fail(CPQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(m)};
     const cuuint64_t strides[1] = {cuuint64_t(k) * 2};
-    const cuuint32_t box[2] = {cuuint32_t(kTcK), cuuint32_t(tile_n)};
+    const cuuint32_t box[2] = {cuuint32_t(kTcAtomK), cuuint32_t(tile_n)};
     const cuuint32_t estr[2] = {1, 1};
     CUtensorMap t;
     const CUresult r = enc(&t, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(x), dims, strides, box, estr,
@@ -529,9 +529,31 @@ static cpq_status run_q4k_mma(const GemvArgs &g, const float *x, int64_t x_strid
     return CPQ_SUCCESS;
 }
 
+// Launch with programmatic serialization and a (2, 1, 1) thread-block cluster.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pair(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                               Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // M > 16 (chunked prefill): X is Q8_K-quantized once into fp16 d*q, then each
-// weight runs as one tcgen05 GEMM launch (gemm_tc.cuh). Token tiles are as
-// few as possible and balanced (tile_n a multiple of 16, at most 256).
+// weight runs as one tcgen05 GEMM launch (gemm_tc.cuh) over CTA pairs. Token
+// tiles are as few as possible and balanced (tile_n a multiple of 32, at
+// most 256).
 static cpq_status run_q4k_tc(const GemvArgs &g, const float *x, int64_t x_stride, int64_t m, uint8_t *ws,
                              cudaStream_t st) {
     const int64_t k = g.k, nbk = k / kQK_K;
@@ -545,7 +567,8 @@ static cpq_status run_q4k_tc(const GemvArgs &g, const float *x, int64_t x_stride
         set[dev].store(1, std::memory_order_relaxed);
     }
     const int64_t n_tok_tiles = (m + kTcMaxTok - 1) / kTcMaxTok;
-    const int tile_n = int(align_up(size_t((m + n_tok_tiles - 1) / n_tok_tiles), 16));
+    const int tile_n = int(align_up(size_t((m + n_tok_tiles - 1) / n_tok_tiles), 32));
+    if (n_tok_tiles > 65535) return fail(CPQ_ERR_UNSUPPORTED, "M=%lld tokens is too many for one call", (long long)m);
     __half *xh = reinterpret_cast<__half *>(ws + kWsActOffset);
 
     const int64_t qwarps = m * nbk;
@@ -555,7 +578,7 @@ static cpq_status run_q4k_tc(const GemvArgs &g, const float *x, int64_t x_stride
 
     static thread_local TcArgs a;
     std::memset(&a, 0, sizeof a);
-    cpq_status rc = f16_act_tensor_map(xh, k, m, tile_n, &a.tmap_x);
+    cpq_status rc = f16_act_tensor_map(xh, k, m, tile_n / 2, &a.tmap_x);
     if (rc) return rc;
     a.m = m;
     a.nbk = int(nbk);
@@ -563,12 +586,14 @@ static cpq_status run_q4k_tc(const GemvArgs &g, const float *x, int64_t x_stride
     for (int i = 0; i < g.n_w; i++) {
         const int64_t n = g.row_start[i + 1] - g.row_start[i];
         if (n == 0) continue;
+        const int64_t pairs = (n + 2 * kTcRows - 1) / (2 * kTcRows);
+        if (pairs > 65535) return fail(CPQ_ERR_UNSUPPORTED, "N=%lld rows is too many for one call", (long long)n);
         if ((rc = q4k_tensor_map(g.w[i], n, k, g.rs, &a.tmap_w, kTcRows, 1))) return rc;
         a.y = g.y[i];
         a.y_stride = g.y_stride[i];
         a.n = n;
-        const dim3 grid(unsigned(n_tok_tiles), unsigned((n + kTcRows - 1) / kTcRows));
-        e = launch(gemm_q4k_tc_kernel, grid, dim3(kTcThreads), size_t(kTcSmem), st, a);
+        e = launch_pair(gemm_q4k_tc_kernel, dim3(2, unsigned(n_tok_tiles), unsigned(pairs)), dim3(kTcThreads),
+                        size_t(kTcSmem), st, a);
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core gemm launch");
     }
     return CPQ_SUCCESS;

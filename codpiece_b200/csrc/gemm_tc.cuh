@@ -15,31 +15,44 @@
 // pairs with one mask each (bits 0-3|16-19 and, shifted by 8, 8-11|24-27).
 // The dot product is unchanged because A and B use the same order.
 //
-// One CTA computes a 128-row x tile_n-token tile of Y (tile_n a multiple of
-// 16, at most 256) over the whole K, in stages of 64 K elements. The
-// dequantized weights (operand A) never touch shared memory: they are
-// written to tensor memory with tcgen05.st and the MMA reads A from there,
-// which leaves shared-memory bandwidth to the activation operand (B).
-// TMEM: 512 columns = the fp32 accumulator (columns 0-255, lane = tile row,
-// column = token) + kTcAStages A stages of 32 columns (64 fp16 per lane).
-//   warp 0      one lane issues tcgen05.mma.cta_group::1.kind::f16 with A in
-//               TMEM and B in shared memory, 4 x K=16 per stage, and commits
-//               each stage back to the "emptyA"/"emptyB" barriers
-//   warp 1      one lane TMA-loads the activation stage (box 64 x tile_n fp16,
-//               SWIZZLE_128B K-major, no multicast) onto "fullB"
-//   warp 2      one lane TMA-loads the tile's raw Q4_K superblocks (box 128
-//               rows x 144 bytes) into the raw ring ("rawFull"/"rawEmpty")
-//   warps 4-11  dequantize: warp w owns TMEM lanes (tile rows) 32*(w%4)..+31,
-//               warps 4-7 the even stages, 8-11 the odd ones; a thread turns
-//               its row's 32 bytes of nibbles into 64 fp16 and stores them as
-//               32 columns with tcgen05.st; the warp arrives on "fullA".
-//               After the K loop they read the accumulator (tcgen05.ld
-//               32x32b), warps 4-7 the first half of the token columns, 8-11
-//               the second, and store Y.
+// A cluster of two CTAs (one per SM) computes a 256-row x tile_n-token tile
+// of Y (tile_n a multiple of 32, at most 256) over the whole K, in stages of
+// 128 K elements (half a superblock; 8 MMAs per stage, which keeps the
+// tensor pipe busy across the per-stage barrier round trip), with 2-SM MMAs (tcgen05.mma.cta_group::2, M = 256): CTA
+// rank r owns weight rows 128r..128r+127 of the pair and tokens
+// tile_n/2*r.. of the activation tile; the pair's tensor cores share both
+// halves of the activation operand, so each SM stores and reads only half
+// of it. The dequantized weights (operand A) never touch shared memory: each
+// CTA writes its rows into its own tensor memory with tcgen05.st and the MMA
+// reads A from there.
+// TMEM per CTA: 512 columns = the fp32 accumulator (columns 0-255, lane =
+// the CTA's tile row, column = token) + kTcAStages A stages of 64 columns.
+//   warp 0      (rank 0 only) one lane issues the MMAs, 8 x K=16 per stage, and
+//               commits each stage to the "emptyA"/"emptyB" barriers of both
+//               CTAs (multicast commit)
+//   warp 1      one lane TMA-loads this CTA's half of the activation stage (two
+//               boxes of 64 x tile_n/2 fp16, one per 128-byte swizzle atom,
+//               SWIZZLE_128B K-major, 2-SM form, no multicast); both CTAs'
+//               loads complete on rank 0's "fullB"
+//   warp 2      one lane TMA-loads this CTA's raw Q4_K superblocks (box 128
+//               rows x 144 bytes) into its raw ring ("rawFull"/"rawEmpty")
+//   warps 4-11  dequantize: warp w owns TMEM lanes (rows) 32*(w%4)..+31, warps
+//               4-7 the first half of every superblock (even stages), 8-11
+//               the second half (odd stages); a thread turns its row's 64
+//               bytes of nibbles into 128 fp16 and stores them as 64 columns
+//               with tcgen05.st; each warp arrives on rank 0's
+//               "fullA" (8 arrivals per stage, 4 per CTA; a plain remote
+//               arrive: the operand lives in tensor memory, ordered by the
+//               tcgen05 fences, so no cluster-scope memory fence is needed).
+//               After the K loop they read
+//               the CTA's accumulator (tcgen05.ld 32x32b), warps 4-7 the first
+//               half of the token columns, 8-11 the second, and store Y.
 // Waits are bounded (kWaitLimitNs); a timeout sets g_dev_error and a CTA-wide
 // abort flag, every role skips to the end, the TMA lanes wait (bounded) for
-// their copies in flight, the MMA lane for its last commit, and warp 0 frees
-// the TMEM columns.
+// their copies in flight, the MMA lane for its last commit, and the TMEM is
+// released after a cluster barrier. CTAs that start after any wait of the
+// device has timed out skip their work (the result is then reported through
+// cpq_device_status).
 #pragma once
 
 #include <cuda.h>
@@ -50,9 +63,10 @@
 
 namespace cpq {
 
-constexpr int kTcRows = 128;      // weight rows per tile (MMA M)
-constexpr int kTcMaxTok = 256;    // tokens per tile at most (MMA N)
-constexpr int kTcK = 64;          // K elements per stage
+constexpr int kTcRows = 128;      // weight rows per CTA (the pair's MMA has M = 256)
+constexpr int kTcMaxTok = 256;    // tokens per pair tile at most (MMA N)
+constexpr int kTcK = 128;         // K elements per stage (two 64-element swizzle atoms)
+constexpr int kTcAtomK = 64;      // K elements per 128-byte swizzle atom
 #ifndef CPQ_TC_A_STAGES
 #define CPQ_TC_A_STAGES 4
 #endif
@@ -60,33 +74,35 @@ constexpr int kTcK = 64;          // K elements per stage
 #define CPQ_TC_B_STAGES 4
 #endif
 #ifndef CPQ_TC_RAW_SLOTS
-#define CPQ_TC_RAW_SLOTS 3
+#define CPQ_TC_RAW_SLOTS 4
 #endif
-constexpr int kTcAStages = CPQ_TC_A_STAGES;    // dequantized weight stages in TMEM (32 columns each)
-constexpr int kTcBStages = CPQ_TC_B_STAGES;    // activation stages in shared memory (32 KB each)
+constexpr int kTcAStages = CPQ_TC_A_STAGES;    // dequantized weight stages in TMEM (64 columns each)
+constexpr int kTcBStages = CPQ_TC_B_STAGES;    // activation half-stages in shared memory (32 KB each)
 constexpr int kTcRawSlots = CPQ_TC_RAW_SLOTS;  // raw superblock slots in shared memory (18 KB each)
 constexpr uint32_t kTcAccCols = 256;           // accumulator columns (tile_n <= 256)
 constexpr uint32_t kTcTmemCols = 512;
-static_assert(kTcAccCols + 32 * kTcAStages <= kTcTmemCols, "TMEM columns");
+constexpr uint32_t kTcAStageCols = kTcK / 2;  // two fp16 per 32-bit column
+static_assert(kTcAccCols + kTcAStageCols * kTcAStages <= kTcTmemCols, "TMEM columns");
 constexpr int kTcThreads = 384;  // 4 role warps + 8 dequantizing warps
 constexpr int kTcDqWarps = 8;
-constexpr int kTcBBytes = kTcMaxTok * 128;
+constexpr int kTcBAtomBytes = kTcMaxTok / 2 * 128;  // one swizzle atom column of the CTA's half
+constexpr int kTcBBytes = kTcBAtomBytes * (kTcK / kTcAtomK);
 constexpr int kTcRawBytes = kTcRows * kQ4K_Bytes;
 constexpr int kTcBarOffset = kTcBStages * kTcBBytes + kTcRawSlots * kTcRawBytes;
-constexpr int kTcSmem = kTcBarOffset + 256 /* barriers, TMEM slot, abort flag */ + 1024 /* alignment slack */;
+constexpr int kTcBarBytes = int(align_up((2 * (kTcAStages + kTcBStages + kTcRawSlots) + 1) * 8 + 8, 128));
+constexpr int kTcSmem = kTcBarOffset + kTcBarBytes /* barriers, TMEM slot, abort flag */ + 1024 /* alignment slack */;
 static_assert(kTcRawBytes % 1024 == 0 && kTcBBytes % 1024 == 0, "1024-byte stage bases");
 static_assert(kTcSmem <= 227 * 1024, "shared memory");
-static_assert((2 * (kTcAStages + kTcBStages + kTcRawSlots) + 1) * 8 + 8 <= 256, "barrier area");
 
 struct alignas(64) TcArgs {
-    CUtensorMap tmap_x;  // fp16 activations [m][k], box 64 x tile_n, SWIZZLE_128B
+    CUtensorMap tmap_x;  // fp16 activations [m][k], box 64 x tile_n/2 (one atom), SWIZZLE_128B
     CUtensorMap tmap_w;  // Q4_K rows as u64 [n][k/256*18], box 18 x 128
     float *y;            // [m][y_stride]
     int64_t y_stride;
     int64_t n;           // weight rows
     int64_t m;           // tokens
     int nbk;             // superblocks per row
-    int tile_n;          // tokens per tile (multiple of 16, 16..256)
+    int tile_n;          // tokens per pair tile (multiple of 32, 32..256)
 };
 
 // ---- tcgen05 / descriptor helpers ------------------------------------------
@@ -107,22 +123,50 @@ __host__ __device__ constexpr uint32_t tc_idesc_f16(int m, int n) {
     return (1u << 4) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
-// D (TMEM) (+)= A (TMEM, K-major: lane = row, two 16-bit K elements per
-// 32-bit column) x B (shared-memory descriptor).
-__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                              uint32_t accumulate) {
+// 2-SM MMA issued by rank 0: D (TMEM of both CTAs) (+)= A (TMEM of both CTAs,
+// K-major: lane = row, two 16-bit K elements per 32-bit column) x B (the two
+// CTAs' shared-memory halves at the same descriptor address).
+__device__ __forceinline__ void tc_mma2_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
-// Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
-__device__ __forceinline__ void tc_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-                 : "memory");
+// Arrive on `bar` in both CTAs of the pair once every tcgen05 operation this
+// thread issued so far has completed.
+__device__ __forceinline__ void tc_commit2(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_addr(bar)),
+        "h"(uint16_t(3))
+        : "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// The shared::cluster address of `p`'s counterpart in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (this CTA's or
+// the peer's), with the default (CTA-scope) release semantics.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -134,6 +178,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
             smem_addr(dst)),
         "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Same into this CTA's shared memory, completing on an mbarrier of either CTA
+// of the pair (2-SM form; bar_caddr is a shared::cluster address). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int x, int y, uint32_t bar_caddr) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(bar_caddr)
         : "memory");
 }
 
@@ -199,8 +253,8 @@ __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<co
 
 // ---- the kernel -------------------------------------------------------------
 
-// grid: (token tiles, row tiles) — the token tiles of one weight tile run
-// side by side, so its raw bytes come from HBM about once.
+// grid: (2, token tiles, row-pair tiles), cluster (2, 1, 1) — the token tiles
+// of one weight tile run side by side, so its raw bytes come from HBM about once.
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid_constant__ TcArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -214,18 +268,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile_n = a.tile_n;
-    const int64_t tok0 = int64_t(blockIdx.x) * tile_n;
-    const int64_t row0 = int64_t(blockIdx.y) * kTcRows;
-    const int nk = a.nbk * 4;
+    const uint32_t rank = cluster_ctarank();
+    const int tile_n = a.tile_n, half_n = tile_n / 2;
+    const int64_t tok0 = int64_t(blockIdx.y) * tile_n;
+    const int64_t row0 = int64_t(blockIdx.z) * (2 * kTcRows) + int64_t(rank) * kTcRows;
+    const int nk = a.nbk * (kQK_K / kTcK);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcAStages; s++) {
-            mbar_init(&fullA[s], kTcDqWarps / 2);  // the 4 warps that dequantize stage s
+            mbar_init(&fullA[s], kTcDqWarps);  // rank 0: 4 warps of each CTA per stage
             mbar_init(&emptyA[s], 1);
         }
         for (int s = 0; s < kTcBStages; s++) {
-            mbar_init(&fullB[s], 1);
+            mbar_init(&fullB[s], 1);  // rank 0: its producer's arrive + both halves' bytes
             mbar_init(&emptyB[s], 1);
         }
         for (int s = 0; s < kTcRawSlots; s++) {
@@ -233,17 +288,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
             mbar_init(&rawEmpty[s], kTcDqWarps);
         }
         mbar_init(done, 1);
-        *abort_flag = 0;
+        // a wait on this device has already timed out: do no work (the error stays reported)
+        *abort_flag = (*reinterpret_cast<volatile uint32_t *>(&g_dev_error) & kDevErrWaitTimeout) ? 1 : 0;
         fence_mbar_init();
     }
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
                      "r"(kTcTmemCols)
                      : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;  // lane 0, column base: accumulator at +0, A stages at +kTcAccCols
 
@@ -251,41 +307,49 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
     pdl_launch_dependents();
 
     if (warp == 0) {
-        // ---- MMA issue ----
-        if (lane == 0) {
-            const uint32_t idesc = tc_idesc_f16(kTcRows, tile_n);
+        // ---- MMA issue (rank 0) ----
+        if (rank == 0 && lane == 0) {
+            const uint32_t idesc = tc_idesc_f16(2 * kTcRows, tile_n);
             for (int t = 0; t < nk; t++) {
                 const int sa = t % kTcAStages, sb = t % kTcBStages;
                 if (!tc_wait(&fullA[sa], uint32_t(t / kTcAStages) & 1u, abort_flag) ||
                     !tc_wait(&fullB[sb], uint32_t(t / kTcBStages) & 1u, abort_flag))
                     break;
                 tc_fence_after();
-                const uint32_t at = tmem + kTcAccCols + 32u * uint32_t(sa);
-                const uint64_t bd = smem_desc_sw128(smem_addr(sB + sb * kTcBBytes));
+                const uint32_t at = tmem + kTcAccCols + kTcAStageCols * uint32_t(sa);
+                const uint64_t bd0 = smem_desc_sw128(smem_addr(sB + sb * kTcBBytes));
+                const uint64_t bd1 = smem_desc_sw128(smem_addr(sB + sb * kTcBBytes + kTcBAtomBytes));
 #pragma unroll
-                for (int kk = 0; kk < kTcK / 16; kk++)  // K=16 per MMA: 8 TMEM columns of A, 32 bytes of B (+2)
-                    tc_mma_f16_ts(tmem, at + 8u * uint32_t(kk), bd + 2 * kk, idesc, (t | kk) != 0 ? 1u : 0u);
-                tc_commit(&emptyA[sa]);
-                tc_commit(&emptyB[sb]);
+                for (int kk = 0; kk < kTcK / 16; kk++)  // K=16 per MMA: 8 TMEM columns of A, 32 bytes of a B atom (+2)
+                    tc_mma2_f16_ts(tmem, at + 8u * uint32_t(kk), (kk < 4 ? bd0 : bd1) + 2 * (kk & 3), idesc,
+                                   (t | kk) != 0 ? 1u : 0u);
+                tc_commit2(&emptyA[sa]);
+                tc_commit2(&emptyB[sb]);
             }
-            tc_commit(done);
-            mbar_wait_bounded(done, 0);  // the accumulator is final (or idle) before TMEM is released
+            tc_commit2(done);
+            mbar_wait_bounded(done, 0);  // the accumulators are final (or idle) before TMEM is released
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ---- activation stages (TMA) ----
+        // ---- this CTA's half of the activation stages (TMA, completing on rank 0) ----
         if (lane == 0) {
             int t = 0;
             for (; t < nk; t++) {
                 const int s = t % kTcBStages;
                 const uint32_t ph = uint32_t(t / kTcBStages) & 1u;
-                if (!tc_wait(&emptyB[s], ph ^ 1u, abort_flag)) break;
-                mbar_arrive_expect_tx(&fullB[s], uint32_t(tile_n) * 128u);
-                tma_load_2d(sB + s * kTcBBytes, &a.tmap_x, t * kTcK, int(tok0), &fullB[s]);
+                if (*abort_flag || !tc_wait(&emptyB[s], ph ^ 1u, abort_flag)) break;
+                if (rank == 0) mbar_arrive_expect_tx(&fullB[s], uint32_t(tile_n) * 2u * kTcK);
+                const uint32_t bar0 = cluster_addr(&fullB[s], 0);
+#pragma unroll
+                for (int at = 0; at < kTcK / kTcAtomK; at++)
+                    tma_load_2d_pair(sB + s * kTcBBytes + at * kTcBAtomBytes, &a.tmap_x, t * kTcK + at * kTcAtomK,
+                                     int(tok0) + int(rank) * half_n, bar0);
             }
-            // no copy may land after the CTA has exited: wait for the last ones issued
-            for (int u = t > kTcBStages ? t - kTcBStages : 0; u < t; u++)
-                mbar_wait_bounded(&fullB[u % kTcBStages], uint32_t(u / kTcBStages) & 1u);
+            // no copy may land after the CTAs have exited: rank 0 waits for the last stages issued
+            // (their barriers count both halves)
+            if (rank == 0)
+                for (int u = t > kTcBStages ? t - kTcBStages : 0; u < t; u++)
+                    mbar_wait_bounded(&fullB[u % kTcBStages], uint32_t(u / kTcBStages) & 1u);
         }
         __syncwarp();
     } else if (warp == 2) {
@@ -295,7 +359,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
             for (; kb < a.nbk; kb++) {
                 const int s = kb % kTcRawSlots;
                 const uint32_t ph = uint32_t(kb / kTcRawSlots) & 1u;
-                if (!tc_wait(&rawEmpty[s], ph ^ 1u, abort_flag)) break;
+                if (*abort_flag || !tc_wait(&rawEmpty[s], ph ^ 1u, abort_flag)) break;
                 mbar_arrive_expect_tx(&rawFull[s], uint32_t(kTcRawBytes));
                 tma_load_2d(sRaw + s * kTcRawBytes, &a.tmap_w, kb * (kQ4K_Bytes / 8), int(row0), &rawFull[s]);
             }
@@ -306,7 +370,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
     } else if (warp >= 4) {
         // ---- dequantization (rows past n arrive zero-filled, so they dequantize to 0) ----
         const int dq = warp - 4;
-        const int grp = dq >> 2;                      // this warp's stages: t % 2 == grp
+        const int grp = dq >> 2;                      // superblock half (= stage parity) of this warp
         const int quarter = warp & 3;                 // TMEM lane quarter this warp may access
         const int r = 32 * quarter + lane;            // tile row = TMEM lane
         const uint32_t lane_base = uint32_t(32 * quarter) << 16;
@@ -314,53 +378,54 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
         for (int t = grp; t < nk; t += 2) {
             const int sa = t % kTcAStages;
             const uint32_t pa = uint32_t(t / kTcAStages) & 1u;
-            const int kb = t >> 2, j = t & 3;
+            const int kb = t >> 1;
             const int rs = kb % kTcRawSlots;
-            if (j == grp) {  // this group's first stage of the superblock
-                ok = __all_sync(0xffffffffu, tc_wait(&rawFull[rs], uint32_t(kb / kTcRawSlots) & 1u, abort_flag));
-                if (!ok) break;
-            }
+            ok = __all_sync(0xffffffffu, tc_wait(&rawFull[rs], uint32_t(kb / kTcRawSlots) & 1u, abort_flag));
+            if (!ok) break;
             const uint8_t *raw = sRaw + rs * kTcRawBytes + r * kQ4K_Bytes;
             const uint4 hd = *reinterpret_cast<const uint4 *>(raw);
-            const uint4 qa = *reinterpret_cast<const uint4 *>(raw + 16 + 32 * j);
-            const uint4 qb = *reinterpret_cast<const uint4 *>(raw + 32 + 32 * j);
-            if (j == 2 + grp) {  // this group's last read of the superblock: hand the slot back
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&rawEmpty[rs]);
-            }
-            // scales/mins of sub-blocks 2j (low nibbles) and 2j+1 (high nibbles): get_scale_min_k4
-            const uint32_t scw = j < 2 ? (hd.y & 0x3f3f3f3fu) : ((hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u));
+            uint4 qv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) qv[i] = *reinterpret_cast<const uint4 *>(raw + 16 + 64 * grp + 16 * i);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&rawEmpty[rs]);  // this warp is done with the superblock
+            // scales/mins of sub-blocks 4*grp .. 4*grp+3 (get_scale_min_k4): bytes of these words
+            const uint32_t scw = grp == 0 ? (hd.y & 0x3f3f3f3fu) : ((hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u));
             const uint32_t mnw =
-                j < 2 ? (hd.z & 0x3f3f3f3fu) : (((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u));
-            const int sh = 16 * (j & 1);
+                grp == 0 ? (hd.z & 0x3f3f3f3fu) : (((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u));
             const float d = half_bits_to_float(hd.x), dmin = half_bits_to_float(hd.x >> 16);
-            const __half2 slo = __float2half2_rn(d * float((scw >> sh) & 0xffu));
-            const __half2 shi = __float2half2_rn(d * float((scw >> (sh + 8)) & 0xffu));
-            const __half2 mlo = __float2half2_rn(-(dmin * float((mnw >> sh) & 0xffu)));
-            const __half2 mhi = __float2half2_rn(-(dmin * float((mnw >> (sh + 8)) & 0xffu)));
-            const uint32_t wq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-            // word i holds elements 4i..4i+3 of sub-block 2j (low nibbles) and of 2j+1
-            // (high nibbles). Stage columns 0-15 are sub-block 2j, 16-31 sub-block 2j+1;
-            // word 2c+h fills columns 4c+2h (its elements 0, 2) and 4c+2h+1 (1, 3)
-            uint32_t v[32];
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const uint32_t w = wq[2 * c + h];
-                    v[4 * c + 2 * h] = h2u(__hfma2(nib2h(w), slo, mlo));
-                    v[4 * c + 2 * h + 1] = h2u(__hfma2(nib2h(w >> 8), slo, mlo));
-                    v[16 + 4 * c + 2 * h] = h2u(__hfma2(nib2h(w >> 4), shi, mhi));
-                    v[16 + 4 * c + 2 * h + 1] = h2u(__hfma2(nib2h(w >> 12), shi, mhi));
-                }
-            }
             ok = __all_sync(0xffffffffu, tc_wait(&emptyA[sa], pa ^ 1u, abort_flag));
             if (!ok) break;
             tc_fence_after();  // the MMAs that read this A stage have completed
-            tmem_st32(tmem + lane_base + kTcAccCols + 32u * uint32_t(sa), v);
+#pragma unroll
+            for (int p = 0; p < 2; p++) {
+                // 32 bytes of nibbles: low nibbles = sub-block 4*grp+2p, high = 4*grp+2p+1
+                const int sh = 16 * p;
+                const __half2 slo = __float2half2_rn(d * float((scw >> sh) & 0xffu));
+                const __half2 shi = __float2half2_rn(d * float((scw >> (sh + 8)) & 0xffu));
+                const __half2 mlo = __float2half2_rn(-(dmin * float((mnw >> sh) & 0xffu)));
+                const __half2 mhi = __float2half2_rn(-(dmin * float((mnw >> (sh + 8)) & 0xffu)));
+                const uint4 qa = qv[2 * p], qb = qv[2 * p + 1];
+                const uint32_t wq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                // columns 0-15: the low sub-block, 16-31: the high one; word 2c+h fills
+                // columns 4c+2h (its elements 0, 2) and 4c+2h+1 (elements 1, 3)
+                uint32_t v[32];
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const uint32_t w = wq[2 * c + h];
+                        v[4 * c + 2 * h] = h2u(__hfma2(nib2h(w), slo, mlo));
+                        v[4 * c + 2 * h + 1] = h2u(__hfma2(nib2h(w >> 8), slo, mlo));
+                        v[16 + 4 * c + 2 * h] = h2u(__hfma2(nib2h(w >> 4), shi, mhi));
+                        v[16 + 4 * c + 2 * h + 1] = h2u(__hfma2(nib2h(w >> 12), shi, mhi));
+                    }
+                }
+                tmem_st32(tmem + lane_base + kTcAccCols + kTcAStageCols * uint32_t(sa) + 32u * uint32_t(p), v);
+            }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&fullA[sa]);
+            if (lane == 0) mbar_arrive_remote(cluster_addr(&fullA[sa], 0));
         }
 
         // ---- epilogue: TMEM lane = tile row, column = token ----
@@ -385,10 +450,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
     }
 
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();  // neither CTA releases TMEM or exits while the pair's MMAs may still use it
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
     }
 }
 
