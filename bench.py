@@ -19,9 +19,20 @@ exactly BASELINE config 2's Q4_K mat-vec shapes, 64 times over.
   cpu_baseline  the CPU oracle (restated ggml-cpu semantics, AVX2 + OpenMP)
              on config 2's three matrices at M = 1, rank 0 at N = 1
 
+  prefill    BASELINE config 4: the Q4_K prefill GEMM on tcgen05
+             at M = 512 and 2048 for both FFN shapes, TFLOP/s through
+             mul_mat (activation pre-pass included) against
+             MEASURED_PEAKS.json bf16_tflops
+
 --impl reference times the reference's CPU path for this operator (the
 oracle restatement: ggml itself is not available) on a bounded sample of the
 same stack (a few layers per step) and prints the same metric.
+
+--profile CASE runs one small fixed case for ncu, its measured launches
+inside an NVTX range named "step" (ncu --nvtx --nvtx-include step/):
+  decode_ffn   Q4_K mul_mat M=1 on config 2's gate and down shapes, 2 calls each
+  prefill_512  Q4_K mul_mat M=512 on [17408 x 5120], 1 call
+  stack        --steps replays of the captured stack decode step
 """
 from __future__ import annotations
 
@@ -47,12 +58,24 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def tensor_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured (burst)"
+    return FALLBACK_BF16_TFLOPS, "fallback"
 
 
 class ClockSampler:
@@ -183,6 +206,97 @@ def kernel_roofline(torch, mm, stream, sets: int = 4, reps: int = 20):
             "launches_timed": reps * len(ws)}
 
 
+def prefill_roofline(torch, mm, reps: int = 10):
+    """Q4_K prefill mul_mat TFLOP/s (tcgen05 GEMM + its activation pre-pass)."""
+    peak, kind = tensor_peak()
+    cases = []
+    cur = torch.cuda.current_stream()
+    for m in (512, 2048):
+        for n, k in ((17408, 5120), (5120, 17408)):
+            ws = [mm.synth_weights(mm.TYPE_Q4_K, k, n, seed=7000 + i) for i in range(2)]
+            x = torch.randn(m, k, device="cuda")
+            y = torch.empty(m, n, device="cuda")
+            for _ in range(3):
+                for w in ws:
+                    mm.mul_mat(w, x, out=y)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            for _ in range(reps):
+                for w in ws:
+                    mm.mul_mat(w, x, out=y)
+            e1.record(cur)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * len(ws))
+            tf = 2.0 * m * n * k / us / 1e6
+            cases.append({"m": m, "n": n, "k": k, "us": round(us, 2), "tflops": round(tf, 1)})
+            del ws, x, y
+    best = max(cases, key=lambda c: c["tflops"])
+    tot_flop = sum(2.0 * c["m"] * c["n"] * c["k"] for c in cases)
+    tot_us = sum(c["us"] for c in cases)
+    ach = tot_flop / tot_us / 1e6
+    return {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(ach / peak, 4), "peak_kind": kind,
+            "kernel": "Q4_K mul_mat M>16: act_f16_kernel + gemm_q4k_tc_kernel (2-SM tcgen05, fp16 operands, "
+                      "fp32 TMEM accumulators)",
+            "achieved_is": "FLOP-weighted over the four configs[3] cases", "best": best, "cases": cases}
+
+
+def profile_case(args) -> int:
+    """One small fixed case for ncu (see the module docstring)."""
+    import torch
+
+    torch.cuda.set_device(0)
+    from codpiece_b200 import build as cbuild
+    if not cbuild.LIB.exists():
+        cbuild.build()
+    from codpiece_b200 import mul_mat as mm
+    mm.init(0, 1 << 30)
+    nvtx = torch.cuda.nvtx
+    if args.profile == "decode_ffn":
+        calls = [(mm.synth_weights(mm.TYPE_Q4_K, k, n, seed=11 + i), torch.randn(1, k, device="cuda"))
+                 for i, (n, k) in enumerate(((17408, 5120), (5120, 17408)))]
+        for w, x in calls:
+            mm.mul_mat(w, x)
+        torch.cuda.synchronize()
+        nvtx.range_push("step")
+        for _ in range(2):
+            for w, x in calls:
+                mm.mul_mat(w, x)
+        torch.cuda.synchronize()
+        nvtx.range_pop()
+    elif args.profile == "prefill_512":
+        w = mm.synth_weights(mm.TYPE_Q4_K, 5120, 17408, seed=21)
+        x = torch.randn(512, 5120, device="cuda")
+        mm.mul_mat(w, x)
+        torch.cuda.synchronize()
+        nvtx.range_push("step")
+        mm.mul_mat(w, x)
+        torch.cuda.synchronize()
+        nvtx.range_pop()
+    elif args.profile == "stack":
+        from codpiece_b200 import stack as st
+        from codpiece_b200 import tp
+        stack = st.Stack(tp.HP_BENCH_27B, args.layers, 0, 1, None, m=args.m, seed=0)
+        stack.h.copy_(torch.randn(args.m, 5120, device="cuda"))
+        stack.capture()
+        for _ in range(args.warmup):
+            stack.replay()
+        torch.cuda.synchronize()
+        nvtx.range_push("step")
+        for _ in range(args.steps):
+            stack.replay()
+        torch.cuda.synchronize()
+        nvtx.range_pop()
+        stack.release()
+    else:
+        log(f"unknown --profile case {args.profile}")
+        return 2
+    assert mm.device_status(0) == 0
+    log(f"profile case {args.profile}: ok")
+    return 0
+
+
 def reference_arm(args, rank):
     """CPU reference (restated ggml-cpu mul_mat) on a bounded sample of the stack."""
     if rank != 0:
@@ -241,7 +355,11 @@ def main() -> int:
     ap.add_argument("--ref-layers", type=int, default=2)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--profile", default=None, choices=["decode_ffn", "prefill_512", "stack"])
     args = ap.parse_args()
+    if args.profile:
+        return profile_case(args)
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")
         args.warmup = 3
@@ -345,9 +463,11 @@ def main() -> int:
     total_bytes = float(b[0])
     launches = stack.launches_per_step() * args.steps
 
-    roof = None
+    roof = prefill = None
     if rank == 0:
         roof = kernel_roofline(torch, mm, cur)
+        if not args.no_prefill:
+            prefill = prefill_roofline(torch, mm)
     barrier()
 
     stack.release()
@@ -382,6 +502,7 @@ def main() -> int:
         "clocks": clk,
         "roofline": roof,
         "cpu_baseline": cpu,
+        "prefill": prefill,
     }
     print(json.dumps(line), flush=True)
     return 0
