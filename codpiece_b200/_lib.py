@@ -26,7 +26,9 @@ STATUS = {
 # Every symbol include/cpq.h declares (checked by tests/test_abi.py).
 EXPORTED = [
     "cpq_init", "cpq_release", "cpq_mul_mat_workspace_size", "cpq_mul_mat", "cpq_mul_mat_ws",
-    "cpq_mul_mat_multi", "cpq_mul_mat_fused", "cpq_mul_mat_noalloc", "cpq_quantize_act", "cpq_rms_norm", "cpq_swiglu", "cpq_add_inplace", "cpq_argmax",
+    "cpq_mul_mat_multi", "cpq_mul_mat_fused", "cpq_mul_mat_noalloc", "cpq_quantize_act", "cpq_rms_norm",
+    "cpq_swiglu", "cpq_add_inplace", "cpq_argmax",
+    "cpq_decode_plan_create", "cpq_decode_plan_run", "cpq_decode_plan_destroy",
     "cpq_tp_split_state", "cpq_tp_unique_id", "cpq_tp_comm_init", "cpq_tp_allreduce_f32", "cpq_tp_comm_check",
     "cpq_tp_comm_destroy", "cpq_synth_weights", "cpq_device_status", "cpq_last_error", "cpq_status_string",
     "cpq_abi_version",
@@ -50,6 +52,11 @@ class CpqSplitState(C.Structure):
 
 class CpqPrologue(C.Structure):
     _fields_ = [("mode", C.c_int32), ("r", C.c_void_p), ("g", C.c_void_p), ("h_out", C.c_void_p), ("eps", C.c_float)]
+
+
+class CpqDecodePhase(C.Structure):
+    _fields_ = [("mode", C.c_int32), ("n_w", C.c_int32), ("x", C.c_void_p), ("r", C.c_void_p), ("g", C.c_void_p),
+                ("h_out", C.c_void_p), ("eps", C.c_float), ("w", C.POINTER(CpqTensor) * 3), ("y", C.c_void_p * 3)]
 
 
 PRO_NONE, PRO_RMS, PRO_SWIGLU = 0, 1, 2
@@ -88,6 +95,9 @@ def lib() -> C.CDLL:
         "cpq_swiglu": (st, [vp, vp, vp, i64, vp]),
         "cpq_add_inplace": (st, [vp, vp, i64, vp]),
         "cpq_argmax": (st, [vp, i64, i64, vp, vp]),
+        "cpq_decode_plan_create": (st, [P(CpqDecodePhase), C.c_int, C.c_int, P(vp)]),
+        "cpq_decode_plan_run": (st, [vp, vp]),
+        "cpq_decode_plan_destroy": (None, [vp]),
         "cpq_tp_split_state": (CpqSplitState, [C.c_char_p, P(CpqHparams), i64, i64, C.c_int]),
         "cpq_tp_unique_id": (st, [vp]),
         "cpq_tp_comm_init": (st, [P(vp), C.c_int, C.c_int, vp, C.c_int, C.c_int]),

@@ -46,68 +46,30 @@ struct ActPrepArgs {
     uint8_t *out;      // the image (row_act_bytes(k, m) bytes)
 };
 
-// grid: (ceil(nbk / 8), m); block 256 = 8 warps, warp w quantizes block 8*blockIdx.x + w of token blockIdx.y
-__global__ void __launch_bounds__(256) act_prep_kernel(const ActPrepArgs a) {
-    pdl_wait();
-    pdl_launch_dependents();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int t = blockIdx.y;
-    const int64_t k = a.k;
-    const int nbk = int(k / kQK_K);
-    const float *xr = a.x + t * a.x_stride;
-    const float *rr = a.r ? a.r + t * a.x_stride : nullptr;
+template <bool L2>
+__device__ __forceinline__ float4 act_ld4(const float *p) {
+    return L2 ? __ldcg(reinterpret_cast<const float4 *>(p)) : *reinterpret_cast<const float4 *>(p);
+}
 
-    float scale = 1.0f;
-    if (a.mode == kActRms) {
-        __shared__ double part[8];
-        double s = 0.0;
-        for (int64_t i = threadIdx.x; i < k; i += 256) {
-            const float v = rr ? __fadd_rn(xr[i], rr[i]) : xr[i];
-            s += double(__fmul_rn(v, v));
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) part[warp] = s;
-        __syncthreads();
-        double tot = 0.0;
-#pragma unroll
-        for (int w = 0; w < 8; w++) tot += part[w];
-        const float mean = float(tot / double(k));
-        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
-    }
-
-    const int b = blockIdx.x * 8 + warp;
-    if (b >= nbk) return;
+// This lane's 8 elements of block b before scaling: x (PLAIN), x + r (RMS;
+// x when r is null) or silu(x) * r (SWIGLU). L2: read through L2 only (the
+// inputs were written by other SMs in the same launch).
+template <bool L2>
+__device__ __forceinline__ void act_load_v(int mode, const float *xr, const float *rr, int b, float (&v)[8]) {
+    const int lane = threadIdx.x & 31;
     const int64_t e0 = int64_t(b) * kQK_K + lane * 8;
-    float v[8];
-    {
-        const float4 x0 = *reinterpret_cast<const float4 *>(xr + e0);
-        const float4 x1 = *reinterpret_cast<const float4 *>(xr + e0 + 4);
-        v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
-        v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
-    }
-    if (a.mode == kActRms) {
+    const float4 x0 = act_ld4<L2>(xr + e0), x1 = act_ld4<L2>(xr + e0 + 4);
+    v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+    v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+    if (mode == kActRms) {
         if (rr) {
-            const float4 r0 = *reinterpret_cast<const float4 *>(rr + e0);
-            const float4 r1 = *reinterpret_cast<const float4 *>(rr + e0 + 4);
+            const float4 r0 = act_ld4<L2>(rr + e0), r1 = act_ld4<L2>(rr + e0 + 4);
             const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
             for (int e = 0; e < 8; e++) v[e] = __fadd_rn(v[e], rv[e]);
-            if (a.h_out) {
-                float *ho = a.h_out + t * a.x_stride + e0;
-                *reinterpret_cast<float4 *>(ho) = make_float4(v[0], v[1], v[2], v[3]);
-                *reinterpret_cast<float4 *>(ho + 4) = make_float4(v[4], v[5], v[6], v[7]);
-            }
         }
-#pragma unroll
-        for (int e = 0; e < 8; e++) v[e] = __fmul_rn(v[e], scale);
-        if (a.g) {
-#pragma unroll
-            for (int e = 0; e < 8; e++) v[e] = __fmul_rn(v[e], a.g[e0 + e]);
-        }
-    } else if (a.mode == kActSwiglu) {
-        const float4 u0 = *reinterpret_cast<const float4 *>(rr + e0);
-        const float4 u1 = *reinterpret_cast<const float4 *>(rr + e0 + 4);
+    } else if (mode == kActSwiglu) {
+        const float4 u0 = act_ld4<L2>(rr + e0), u1 = act_ld4<L2>(rr + e0 + 4);
         const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
         for (int e = 0; e < 8; e++) {
@@ -115,14 +77,31 @@ __global__ void __launch_bounds__(256) act_prep_kernel(const ActPrepArgs a) {
             v[e] = __fmul_rn(s, uv[e]);
         }
     }
+}
 
+// Block b of token row t from its loaded values v: RMS scaling (and weight
+// g), the Q8_K quantizer, and the three parts of the activation image of m
+// rows (layout above). One warp.
+__device__ __forceinline__ void act_quantize_store(int mode, float (&v)[8], float scale, const float *g, int b, int t,
+                                                   int64_t k, int m, uint8_t *img) {
+    const int lane = threadIdx.x & 31;
+    const int nbk = int(k / kQK_K);
+    const int64_t e0 = int64_t(b) * kQK_K + lane * 8;
+    if (mode == kActRms) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = __fmul_rn(v[e], scale);
+        if (g) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = __fmul_rn(v[e], g[e0 + e]);
+        }
+    }
     int q[8];
     const float d = q8k_quantize_block(v, lane, q);
     uint32_t lo, hi;
     pack8(q, lo, hi);
-    uint8_t *qs = a.out;
-    float *dd = reinterpret_cast<float *>(a.out + align_up(size_t(a.m) * size_t(k), 16));
-    uint8_t *bs = reinterpret_cast<uint8_t *>(dd) + align_up(size_t(a.m) * nbk * 4, 16);
+    uint8_t *qs = img;
+    float *dd = reinterpret_cast<float *>(img + align_up(size_t(m) * size_t(k), 16));
+    uint8_t *bs = reinterpret_cast<uint8_t *>(dd) + align_up(size_t(m) * nbk * 4, 16);
     *reinterpret_cast<uint2 *>(qs + t * k + e0) = make_uint2(lo, hi);
     int s8 = 0;
 #pragma unroll
@@ -135,6 +114,80 @@ __global__ void __launch_bounds__(256) act_prep_kernel(const ActPrepArgs a) {
         bb[8 + (lane >> 2)] = uint8_t(int8_t(s32 >> 8));
     }
     if (lane == 0) dd[t * nbk + b] = d;
+}
+
+__device__ __forceinline__ void store8(float *p, const float (&v)[8]) {
+    *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4 *>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// Blocks a warp handles when a CTA of 8 warps covers a whole row: w, w+8, ...
+constexpr int kActBatch = 5;  // blocks whose loads are in flight together
+
+// RMS scale of one token row, 1/sqrt(mean((x + r)^2) + eps) with ggml-cpu's
+// arithmetic (fp32 squares summed in double), computed by a whole CTA of 256
+// threads. Summation order (fixed, so every caller gets the same bits):
+// lane l of warp w adds, for its blocks b = w, w+8, ... in turn, elements
+// 8l..8l+7 of b; then a butterfly over the warp; then warps 0..7 in order.
+// `part` is 8 doubles of shared scratch. When every warp has at most
+// kActBatch blocks, their values are left in vk (block j of the warp in
+// vk[j]) and the function returns true.
+template <bool L2>
+__device__ __forceinline__ bool act_rms_row(const float *xr, const float *rr, int64_t k, float eps, double *part,
+                                            float &scale, float (&vk)[kActBatch][8]) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nbk = int(k / kQK_K);
+    const int nbw = nbk > warp ? (nbk - warp + 7) / 8 : 0;
+    double s = 0.0;
+    for (int j0 = 0; j0 < nbw; j0 += kActBatch) {
+#pragma unroll
+        for (int jj = 0; jj < kActBatch; jj++)
+            if (j0 + jj < nbw) act_load_v<L2>(kActRms, xr, rr, warp + 8 * (j0 + jj), vk[jj]);
+#pragma unroll
+        for (int jj = 0; jj < kActBatch; jj++)
+            if (j0 + jj < nbw) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) s += double(__fmul_rn(vk[jj][e], vk[jj][e]));
+            }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    __syncthreads();  // part may still be read by a previous call
+    if (lane == 0) part[warp] = s;
+    __syncthreads();
+    double tot = 0.0;
+#pragma unroll
+    for (int w = 0; w < 8; w++) tot += part[w];
+    const float mean = float(tot / double(k));
+    scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    return (nbk + 7) / 8 <= kActBatch;
+}
+
+// grid: (ceil(nbk / 8), m); block 256 = 8 warps, warp w quantizes block 8*blockIdx.x + w of token blockIdx.y
+__global__ void __launch_bounds__(256) act_prep_kernel(const ActPrepArgs a) {
+    // Dependents (the row GEMV) may launch before this kernel even starts
+    // waiting: they only prefetch weights until their own griddepcontrol.wait,
+    // which still orders them after this kernel, and so they take each SM as
+    // soon as the GEMV before this kernel leaves it.
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ double part[8];
+    const int warp = threadIdx.x >> 5;
+    const int t = blockIdx.y;
+    const int nbk = int(a.k / kQK_K);
+    const float *xr = a.x + t * a.x_stride;
+    const float *rr = a.r ? a.r + t * a.x_stride : nullptr;
+    float scale = 1.0f;
+    if (a.mode == kActRms) {
+        float vk[kActBatch][8];
+        act_rms_row<false>(xr, rr, a.k, a.eps, part, scale, vk);
+    }
+    const int b = blockIdx.x * 8 + warp;
+    if (b >= nbk) return;
+    float v[8];
+    act_load_v<false>(a.mode, xr, rr, b, v);
+    if (a.mode == kActRms && rr && a.h_out) store8(a.h_out + t * a.x_stride + int64_t(b) * kQK_K + (threadIdx.x & 31) * 8, v);
+    act_quantize_store(a.mode, v, scale, a.g, b, t, a.k, a.m, a.out);
 }
 
 }  // namespace cpq

@@ -59,6 +59,120 @@ struct alignas(64) RowArgs {
     int *counters;        // [row block], zero between calls
 };
 
+// Lane = row: this lane's 144-byte superblock (h = header, qv = nibbles)
+// against block kb of the activation image, MT tokens, accumulated into acc
+// (ggml_vec_dot_q4_K_q8_K's integer sub-block dots, fp32 per superblock).
+template <int MT>
+__device__ __forceinline__ void row_dot(const uint4 &h, const uint4 (&qv)[8], const int8_t *xs, const float *xd,
+                                        const uint8_t *xb, int64_t k, int nbk, int kb, float (&acc)[MT]) {
+    const uint32_t sca = h.y & 0x3f3f3f3fu, scb = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
+    const uint32_t mna = h.z & 0x3f3f3f3fu, mnb = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
+    const float dw = half_bits_to_float(h.x), dm = half_bits_to_float(h.x >> 16);
+    int isc[MT];
+#pragma unroll
+    for (int t = 0; t < MT; t++) isc[t] = 0;
+#pragma unroll
+    for (int jj = 0; jj < 4; jj++) {
+        const uint4 wa = qv[2 * jj], wb = qv[2 * jj + 1];
+        const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const uint32_t sw = jj < 2 ? sca : scb;
+        const int slo = byte_of(sw, (2 * jj) & 3), shi = byte_of(sw, (2 * jj + 1) & 3);
+#pragma unroll
+        for (int t = 0; t < MT; t++) {
+            const int4 *xp = reinterpret_cast<const int4 *>(xs + t * k + kb * kQK_K + 64 * jj);
+            const int4 x0 = xp[0], x1 = xp[1], x2 = xp[2], x3 = xp[3];
+            const int xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            const int xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+            int dl = 0, dh = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                dl = __dp4a(int(w[i] & 0x0f0f0f0fu), xl[i], dl);
+                dh = dp4a_us(w[i] & 0xf0f0f0f0u, xh[i], dh);  // 16 * q_hi
+            }
+            isc[t] += slo * dl + shi * (dh >> 4);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < MT; t++) {
+        const uint4 bsv = *reinterpret_cast<const uint4 *>(xb + (size_t(t) * nbk + kb) * 16);
+        const int imn = 256 * (__dp4a(int(mna), int(bsv.z), 0) + __dp4a(int(mnb), int(bsv.w), 0)) +
+                        dp4a_uu(mna, bsv.x, dp4a_uu(mnb, bsv.y, 0));
+        const float dx = xd[t * nbk + kb];
+        acc[t] += (dw * dx) * float(isc[t]) - (dm * dx) * float(imn);
+    }
+}
+
+// End of a warp's segment of 32-row block mb (its last superblock, or the end
+// of its stream-K share). A segment covering the whole row block stores Y;
+// otherwise the warp parks its partial sums and the last of the row block's
+// npieces owners (atomic counter, acq_rel) adds them in K order, stores Y and
+// resets the counter. The warp's slot is 0 for the row block it starts in,
+// 1 for any later one (a share spans at most two partial row blocks).
+struct RowSeg {
+    int64_t G, T;          // warps, iterations of the whole split
+    int64_t g;             // this warp
+    int64_t first_mb;      // the row block this warp's share starts in
+    float *partials;       // [warp][2][256]
+    int *counters;         // [row block]
+};
+
+template <int MT>
+__device__ __forceinline__ void row_segment_end(const RowSeg &sg, int64_t mb, int nbk, bool whole, float (&acc)[MT],
+                                                float *y, int64_t y_stride, int m, bool row_ok, int64_t row) {
+    const int lane = threadIdx.x & 31;
+    if (whole) {
+#pragma unroll
+        for (int t = 0; t < MT; t++)
+            if (t < m && row_ok) y[size_t(t) * y_stride + row] = acc[t];
+        return;
+    }
+    const int64_t first = owner_warp(mb * nbk, sg.G, sg.T);
+    const int64_t last = owner_warp(mb * nbk + nbk - 1, sg.G, sg.T);
+    const int npieces = int(last - first + 1);
+    const int my_slot = (mb == sg.first_mb) ? 0 : 1;
+    float *pp = sg.partials + (size_t(sg.g) * 2 + my_slot) * 256;
+#pragma unroll
+    for (int t = 0; t < MT; t++) pp[lane * 4 + t] = acc[t];
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) old = atom_add_acq_rel_gpu(&sg.counters[mb], 1);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    __syncwarp();
+    if (old == npieces - 1) {
+        // Piece p > 0 starts inside this row block (slot 0); piece 0 uses slot 1
+        // when its share began in an earlier row block. The loads of a batch of
+        // pieces are issued together, then added in piece order.
+        const int first_slot = (first * sg.T / sg.G < mb * nbk) ? 1 : 0;
+        constexpr int kBatch = 8;
+        float sum[MT];
+#pragma unroll
+        for (int t = 0; t < MT; t++) sum[t] = 0.0f;
+        for (int p0 = 0; p0 < npieces; p0 += kBatch) {
+            float pv[kBatch][MT];
+#pragma unroll
+            for (int j = 0; j < kBatch; j++) {
+                if (p0 + j < npieces) {
+                    const int sl = (p0 + j == 0) ? first_slot : 0;
+                    const float *q = sg.partials + (size_t(first + p0 + j) * 2 + sl) * 256;
+#pragma unroll
+                    for (int t = 0; t < MT; t++) pv[j][t] = __ldcg(q + lane * 4 + t);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kBatch; j++) {
+                if (p0 + j < npieces) {
+#pragma unroll
+                    for (int t = 0; t < MT; t++) sum[t] += pv[j][t];
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < MT; t++)
+            if (t < m && row_ok) y[size_t(t) * y_stride + row] = sum[t];
+        if (lane == 0) sg.counters[mb] = 0;
+    }
+}
+
 template <int MT>
 __global__ void __launch_bounds__(kRowWarps * 32, 1) gemv_q4k_row_kernel(const __grid_constant__ RowArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -134,6 +248,7 @@ __global__ void __launch_bounds__(kRowWarps * 32, 1) gemv_q4k_row_kernel(const _
     int64_t seg_start = it_begin;
     int slot = 0;
     uint32_t phase = 0;
+    const RowSeg sg{G, T, g, it_begin / nbk, a.partials, a.counters};
     while (c_it < it_end) {
         if (!mbar_wait_bounded(&bars[slot], phase)) {
             // error recorded in the device word: wait (bounded) for this warp's other copies, then leave
@@ -150,41 +265,7 @@ __global__ void __launch_bounds__(kRowWarps * 32, 1) gemv_q4k_row_kernel(const _
         __syncwarp();
         if (p_it < it_end) issue(slot);  // the stage is in registers: refill it now
 
-        const uint32_t sca = h.y & 0x3f3f3f3fu, scb = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
-        const uint32_t mna = h.z & 0x3f3f3f3fu, mnb = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
-        const float dw = half_bits_to_float(h.x), dm = half_bits_to_float(h.x >> 16);
-        int isc[MT];
-#pragma unroll
-        for (int t = 0; t < MT; t++) isc[t] = 0;
-#pragma unroll
-        for (int jj = 0; jj < 4; jj++) {
-            const uint4 wa = qv[2 * jj], wb = qv[2 * jj + 1];
-            const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-            const uint32_t sw = jj < 2 ? sca : scb;
-            const int slo = byte_of(sw, (2 * jj) & 3), shi = byte_of(sw, (2 * jj + 1) & 3);
-#pragma unroll
-            for (int t = 0; t < MT; t++) {
-                const int4 *xp = reinterpret_cast<const int4 *>(xs + t * k + c_kb * kQK_K + 64 * jj);
-                const int4 x0 = xp[0], x1 = xp[1], x2 = xp[2], x3 = xp[3];
-                const int xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                const int xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
-                int dl = 0, dh = 0;
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    dl = __dp4a(int(w[i] & 0x0f0f0f0fu), xl[i], dl);
-                    dh = dp4a_us(w[i] & 0xf0f0f0f0u, xh[i], dh);  // 16 * q_hi
-                }
-                isc[t] += slo * dl + shi * (dh >> 4);
-            }
-        }
-#pragma unroll
-        for (int t = 0; t < MT; t++) {
-            const uint4 bsv = *reinterpret_cast<const uint4 *>(xb + (size_t(t) * nbk + c_kb) * 16);
-            const int imn = 256 * (__dp4a(int(mna), int(bsv.z), 0) + __dp4a(int(mnb), int(bsv.w), 0)) +
-                            dp4a_uu(mna, bsv.x, dp4a_uu(mnb, bsv.y, 0));
-            const float dx = xd[t * nbk + c_kb];
-            acc[t] += (dw * dx) * float(isc[t]) - (dm * dx) * float(imn);
-        }
+        row_dot<MT>(h, qv, xs, xd, xb, k, nbk, c_kb, acc);
 
         c_it++;
         if (++slot == kRowStages) {
@@ -196,40 +277,8 @@ __global__ void __launch_bounds__(kRowWarps * 32, 1) gemv_q4k_row_kernel(const _
             const int wi = weight_of(c_mb);
             const int64_t row0 = (c_mb - a.mb_start[wi]) * kRowRows;
             const bool row_ok = row0 + lane < a.n[wi];
-            if (seg_start == c_mb * nbk && blk_end) {
-#pragma unroll
-                for (int t = 0; t < MT; t++)
-                    if (t < a.m && row_ok) a.y[wi][size_t(t) * a.y_stride[wi] + row0 + lane] = acc[t];
-            } else {
-                const int64_t first = owner_warp(c_mb * nbk, G, T);
-                const int64_t last = owner_warp(c_mb * nbk + nbk - 1, G, T);
-                const int npieces = int(last - first + 1);
-                const int my_slot = (c_mb == it_begin / nbk) ? 0 : 1;
-                float *pp = a.partials + (size_t(g) * 2 + my_slot) * 256;
-#pragma unroll
-                for (int t = 0; t < MT; t++) pp[lane * 4 + t] = acc[t];
-                __syncwarp();
-                int old = 0;
-                if (lane == 0) old = atom_add_acq_rel_gpu(&a.counters[c_mb], 1);
-                old = __shfl_sync(0xffffffffu, old, 0);
-                __syncwarp();
-                if (old == npieces - 1) {
-                    float sum[MT];
-#pragma unroll
-                    for (int t = 0; t < MT; t++) sum[t] = 0.0f;
-                    for (int p = 0; p < npieces; p++) {
-                        const int64_t gp = first + p;
-                        const int sl = (c_mb == (gp * T / G) / nbk) ? 0 : 1;
-                        const float *q = a.partials + (size_t(gp) * 2 + sl) * 256;
-#pragma unroll
-                        for (int t = 0; t < MT; t++) sum[t] += __ldcg(q + lane * 4 + t);
-                    }
-#pragma unroll
-                    for (int t = 0; t < MT; t++)
-                        if (t < a.m && row_ok) a.y[wi][size_t(t) * a.y_stride[wi] + row0 + lane] = sum[t];
-                    if (lane == 0) a.counters[c_mb] = 0;
-                }
-            }
+            row_segment_end<MT>(sg, c_mb, nbk, seg_start == c_mb * nbk && blk_end, acc, a.y[wi], a.y_stride[wi], a.m,
+                                row_ok, row0 + lane);
 #pragma unroll
             for (int t = 0; t < MT; t++) acc[t] = 0.0f;
             seg_start = c_it;

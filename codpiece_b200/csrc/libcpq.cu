@@ -9,12 +9,14 @@
 //   act_prep.cuh     decode activation image: fused rms/swiglu prologue + Q8_K
 //   gemv_row.cuh     Q4_K decode GEMV (M 1..3), lane per row
 //   gemm_tc.cuh      Q4_K chunked-prefill GEMM (M > 16) on tcgen05 tensor cores
+//   decode.cuh       persistent decode step: a chain of Q4_K GEMV phases in one launch
 //   elementwise.cuh  rms norm, SwiGLU, residual add, argmax
 //   synth.cuh        seeded synthetic weights
 //   split.inl        tensor-parallel partition rules (host)
 //   tp.inl           NCCL communicator (host)
 //   api.inl          extern "C" entry points declared in include/cpq.h
 //   noalloc.inl      cpq_mul_mat_noalloc: decode GEMV on static device scratch
+//   plan.inl         cpq_decode_plan_*: host side of the persistent decode kernel
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ < 1000
 #error "libcpq targets sm_100a (B200) only"
 #endif
@@ -23,6 +25,7 @@
 #include <cstring>
 #include <memory>
 #include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "elementwise.cuh"
@@ -31,9 +34,11 @@
 #include "act_prep.cuh"
 #include "gemv_row.cuh"
 #include "gemm_tc.cuh"
+#include "decode.cuh"
 #include "quantize.cuh"
 #include "synth.cuh"
 #include "split.inl"
 #include "tp.inl"
 #include "api.inl"
 #include "noalloc.inl"
+#include "plan.inl"

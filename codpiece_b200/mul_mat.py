@@ -236,3 +236,63 @@ def device_status(device: int = 0, clear: bool = True) -> int:
     if rc not in (0, 7):
         check(rc, "cpq_device_status")
     return word.value
+
+
+@dataclass
+class DecodePhase:
+    """One phase of a decode plan (include/cpq.h cpq_decode_phase): up to three
+    Q4_K weights applied to one input vector through a fused prologue."""
+
+    weights: list
+    outs: list
+    x: torch.Tensor
+    mode: int = PRO_NONE
+    r: torch.Tensor | None = None
+    g: torch.Tensor | None = None
+    h_out: torch.Tensor | None = None
+    eps: float = 1e-6
+
+
+class DecodePlan:
+    """A chain of decode phases run as one persistent kernel (cpq_decode_plan_*).
+
+    The plan bakes in the device pointers of the weights and buffers: keep
+    them alive (this object holds references) and reuse the same buffers
+    every step. run() is capturable in a CUDA graph."""
+
+    def __init__(self, phases: list[DecodePhase], device: int | None = None):
+        dev = torch.cuda.current_device() if device is None else device
+        self._keep = phases
+        self._descs = []
+        arr = (_lib.CpqDecodePhase * len(phases))()
+        for i, ph in enumerate(phases):
+            if not 1 <= len(ph.weights) <= 3 or len(ph.outs) != len(ph.weights):
+                raise ValueError("a decode phase has 1..3 weights and one output per weight")
+            c = arr[i]
+            c.mode, c.n_w = ph.mode, len(ph.weights)
+            c.x, c.r, c.g, c.h_out, c.eps = _ptr(ph.x), _ptr(ph.r), _ptr(ph.g), _ptr(ph.h_out), ph.eps
+            for j, (w, y) in enumerate(zip(ph.weights, ph.outs)):
+                if y.numel() < w.n or not y.is_contiguous():
+                    raise ValueError("decode phase output must be a contiguous vector of N floats")
+                d = w.desc()
+                self._descs.append(d)
+                c.w[j] = C.pointer(d)
+                c.y[j] = y.data_ptr()
+        self._arr = arr
+        self.handle = C.c_void_p()
+        check(lib().cpq_decode_plan_create(arr, len(phases), dev, C.byref(self.handle)), "cpq_decode_plan_create")
+        self.n_phases = len(phases)
+
+    def run(self, stream=None) -> None:
+        check(lib().cpq_decode_plan_run(self.handle, _stream(stream)), "cpq_decode_plan_run")
+
+    def close(self) -> None:
+        if self.handle:
+            lib().cpq_decode_plan_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass

@@ -83,7 +83,8 @@ class Stack:
     """This rank's shard of the stack plus its activation buffers."""
 
     def __init__(self, hp: tp.Hparams, n_layer: int, rank: int = 0, world: int = 1, comm: Comm | None = None,
-                 m: int = 1, seed: int = 0, head: bool = True, device: int | None = None, eps: float = 1e-6):
+                 m: int = 1, seed: int = 0, head: bool = True, device: int | None = None, eps: float = 1e-6,
+                 use_plan: bool = False):
         self.hp, self.n_layer, self.rank, self.world, self.comm, self.m = hp, n_layer, rank, world, comm, m
         self.eps = eps
         self.dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
@@ -128,6 +129,11 @@ class Stack:
         self.tok = torch.zeros(m, dtype=torch.int32, device=self.dev)
         mm.init(self.dev.index, 64 << 20)
         self.graph: torch.cuda.CUDAGraph | None = None
+        self.plan: mm.DecodePlan | None = None
+        if use_plan:
+            if world != 1 or m != 1:
+                raise ValueError("decode plans run the single-GPU M = 1 step")
+            self._build_plan()
 
     # -- bytes -------------------------------------------------------------
     def weight_bytes(self) -> int:
@@ -148,6 +154,8 @@ class Stack:
             return (1 if prologue else 0) + 2 * groups
 
         n = 0
+        if self.plan is not None:
+            return 1 + fused(mm.TYPE_Q6_K, True) + 1 if self.head is not None else 1
         for il, lw in enumerate(self.layers):
             if lw.q is not None or lw.k is not None or lw.v is not None:
                 n += fused(mm.TYPE_Q4_K, True)
@@ -160,6 +168,33 @@ class Stack:
         else:
             n += 1
         return n
+
+    def _build_plan(self) -> None:
+        """The 64-layer trunk of step_body() as one decode plan (4 phases per
+        layer); the head stays a separate fused call + argmax."""
+        phases = []
+        h, h_alt = self.h, self.h_alt
+        part_live = False
+        for lw in self.layers:
+            ws = [w for w in (lw.q, lw.k, lw.v) if w is not None]
+            outs = [self._sl(b, w.n).view(-1) for w, b in ((lw.q, self.qb), (lw.k, self.kb), (lw.v, self.vb))
+                    if w is not None]
+            if part_live:
+                phases.append(mm.DecodePhase(ws, outs, h.view(-1), mm.PRO_RMS, r=self.part.view(-1),
+                                             h_out=h_alt.view(-1), eps=self.eps))
+                h, h_alt = h_alt, h
+            else:
+                phases.append(mm.DecodePhase(ws, outs, h.view(-1), mm.PRO_RMS, eps=self.eps))
+            phases.append(mm.DecodePhase([lw.o], [self.part.view(-1)], self._sl(self.qb, lw.o.k).view(-1)))
+            nf = lw.gate.n
+            g, u = self._sl(self.gb, nf).view(-1), self._sl(self.ub, nf).view(-1)
+            phases.append(mm.DecodePhase([lw.gate, lw.up], [g, u], h.view(-1), mm.PRO_RMS, r=self.part.view(-1),
+                                         h_out=h_alt.view(-1), eps=self.eps))
+            h, h_alt = h_alt, h
+            phases.append(mm.DecodePhase([lw.down], [self.part.view(-1)], g, mm.PRO_SWIGLU, r=u))
+            part_live = True
+        self.plan = mm.DecodePlan(phases, self.dev.index)
+        self._plan_h = (h, h_alt)
 
     # -- one step ----------------------------------------------------------
     def _sl(self, buf: torch.Tensor, n: int) -> torch.Tensor:
@@ -175,7 +210,11 @@ class Stack:
         On return self.h holds the final residual stream."""
         h, h_alt = self.h, self.h_alt
         part_live = False  # self.part holds a projection output still to be added to h
-        for lw in self.layers:
+        if self.plan is not None:
+            self.plan.run()
+            h, h_alt = self._plan_h
+            part_live = len(self.layers) > 0
+        for lw in ([] if self.plan is not None else self.layers):
             # attention block: xn = rms(h [+ part]) -> q, k, v
             ws, outs = [], []
             for w, b in ((lw.q, self.qb), (lw.k, self.kb), (lw.v, self.vb)):
@@ -233,3 +272,6 @@ class Stack:
 
     def release(self) -> None:
         self.graph = None
+        if self.plan is not None:
+            self.plan.close()
+            self.plan = None

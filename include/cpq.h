@@ -159,6 +159,47 @@ cpq_status cpq_add_inplace(float *y, const float *x, int64_t n, void *stream);
  * greedy pick after the LM head (qwen35.rs:2800-2818). */
 cpq_status cpq_argmax(const float *x, int64_t n, int64_t m, int32_t *out, void *stream);
 
+/* ---- decode plans: a whole chain of decode projections in one launch -------
+ *
+ * A decode step (M = 1) is a chain of projections in which each one's input
+ * comes from the previous ones (codpiece's qwen35 trunk, qwen35.rs:2554-2786:
+ * rms -> q/k/v, o, rms -> gate/up, swiglu -> down, per layer). Issued as
+ * separate cpq_mul_mat_fused calls, the weight stream stops at every kernel
+ * boundary. A plan runs the chain as one persistent kernel in which each
+ * SM keeps prefetching the next projections' weights while the current
+ * one's input is being produced. No reference counterpart: this is a graph-
+ * level fusion of consecutive ggml_mul_mat nodes (each phase has exactly the
+ * semantics of one cpq_mul_mat_fused call with M = 1). */
+
+/* One phase: up to three Q4_K weights (same K and row stride) applied to one
+ * input vector through the prologue of cpq_mul_mat_fused. x, r, g, h_out and
+ * the y vectors are device pointers, 16-byte aligned; x and r hold K floats,
+ * y[i] holds N_i = w[i]->ne[1] floats. An input may be the output of an
+ * earlier phase of the same plan; a phase must not write what it reads. */
+typedef struct cpq_decode_phase {
+    int32_t mode;            /* CPQ_PRO_NONE / CPQ_PRO_RMS / CPQ_PRO_SWIGLU */
+    int32_t n_w;             /* 1..3 */
+    const float *x;          /* input [K] */
+    const float *r;          /* RMS: residual added to x (or NULL); SWIGLU: up */
+    const float *g;          /* RMS weight [K] (or NULL) */
+    float *h_out;            /* RMS with r: x + r stored here (or NULL) */
+    float eps;
+    const cpq_tensor *w[3];  /* Q4_K weights */
+    float *y[3];             /* outputs */
+} cpq_decode_phase;
+
+typedef struct cpq_decode_plan cpq_decode_plan;
+
+/* Validates the phases and builds the device-side tables (allocates device
+ * memory: call outside stream capture) for `device`. The pointers are baked
+ * in: the plan is valid while the weights and buffers live. */
+cpq_status cpq_decode_plan_create(const cpq_decode_phase *phases, int n_phases, int device, cpq_decode_plan **plan);
+/* Enqueues the chain on `stream` (capturable; one CTA per SM, cooperative).
+ * Consecutive runs of plans on one device must not overlap on the GPU. */
+cpq_status cpq_decode_plan_run(cpq_decode_plan *plan, void *stream);
+/* Frees the plan (after its last run has completed). NULL is ignored. */
+void cpq_decode_plan_destroy(cpq_decode_plan *plan);
+
 /* ---- tensor parallel ------------------------------------------------------ */
 
 /* Split axis values (crates/codpiece-model/src/split.rs:17-31). */
