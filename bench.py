@@ -356,6 +356,7 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--nccl", action="store_true", help="TP partial sums through NCCL instead of the fused allreduce")
     ap.add_argument("--profile", default=None, choices=["decode_ffn", "prefill_512", "stack"])
     args = ap.parse_args()
     if args.profile:
@@ -396,8 +397,14 @@ def main() -> int:
         dist.broadcast_object_list(obj, src=0)
         comm = st.Comm(world, rank, obj[0], local, timeout_ms=120000)
 
+    def exchange(handle: bytes) -> list:
+        got = [None] * world
+        dist.all_gather_object(got, handle)
+        return got
+
     t_build = time.perf_counter()
-    stack = st.Stack(tp.HP_BENCH_27B, args.layers, rank, world, comm, m=args.m, seed=0)
+    stack = st.Stack(tp.HP_BENCH_27B, args.layers, rank, world, comm, m=args.m, seed=0,
+                     ar_exchange=exchange if (world > 1 and not args.nccl) else None)
     g = torch.Generator(device="cpu").manual_seed(1234)
     h0 = torch.randn(args.m, 5120, generator=g).cuda()
     stack.h.copy_(h0)
@@ -470,6 +477,8 @@ def main() -> int:
             prefill = prefill_roofline(torch, mm)
     barrier()
 
+    ar_mode = ("none" if world == 1 else "nccl" if stack.ar is None else
+               "fused into the GEMV over NVLink peer memory (cpq_mul_mat_fused_ar)")
     stack.release()
     if comm is not None:
         comm.destroy()
@@ -488,7 +497,8 @@ def main() -> int:
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8 dots (Q4_K/Q6_K x Q8_K), fp32 accumulate", "data": "synthetic",
         "config": {"workload": "27B-shaped stack decode (BASELINE config 5): 64 x Q4_K q/k/v/o/gate/up/down + "
-                               "mirrored Q6_K head [151936x5120], M=1, TP=N over NCCL",
+                               "mirrored Q6_K head [151936x5120], M=1, TP=N",
+                   "tp_allreduce": ar_mode,
                    "layers": args.layers, "m": args.m, "tp": world, "hidden": 5120, "ffn": 17408,
                    "vocab": 151936, "parallelism": f"tp{world}",
                    "weight_bytes_all_ranks": int(total_bytes),

@@ -44,6 +44,7 @@ struct ActPrepArgs {
     int m;
     float eps;
     uint8_t *out;      // the image (row_act_bytes(k, m) bytes)
+    ArIn ar;           // RMS: r = the all-reduced residual of this channel (r must be null)
 };
 
 template <bool L2>
@@ -52,17 +53,30 @@ __device__ __forceinline__ float4 act_ld4(const float *p) {
 }
 
 // This lane's 8 elements of block b before scaling: x (PLAIN), x + r (RMS;
-// x when r is null) or silu(x) * r (SWIGLU). L2: read through L2 only (the
-// inputs were written by other SMs in the same launch).
+// x when r is null) or silu(x) * r (SWIGLU). With ar (RMS), r is the sum of
+// the ranks' partial rows in rank order (the fused allreduce). L2: read
+// through L2 only (the inputs were written by other SMs in the same launch).
 template <bool L2>
-__device__ __forceinline__ void act_load_v(int mode, const float *xr, const float *rr, int b, float (&v)[8]) {
+__device__ __forceinline__ void act_load_v(int mode, const float *xr, const float *rr, int b, float (&v)[8],
+                                           const ArRows *ar = nullptr) {
     const int lane = threadIdx.x & 31;
     const int64_t e0 = int64_t(b) * kQK_K + lane * 8;
     const float4 x0 = act_ld4<L2>(xr + e0), x1 = act_ld4<L2>(xr + e0 + 4);
     v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
     v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
     if (mode == kActRms) {
-        if (rr) {
+        if (ar) {
+            float rv[8];
+            ar_words8(ar->p0 + e0, ar->seq, rv);
+            for (int s = 1; s < ar->n; s++) {
+                float q[8];
+                ar_words8(ar->p0 + s * ar->stride + e0, ar->seq, q);
+#pragma unroll
+                for (int e = 0; e < 8; e++) rv[e] = __fadd_rn(rv[e], q[e]);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = __fadd_rn(v[e], rv[e]);
+        } else if (rr) {
             const float4 r0 = act_ld4<L2>(rr + e0), r1 = act_ld4<L2>(rr + e0 + 4);
             const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
@@ -134,7 +148,7 @@ constexpr int kActBatch = 5;  // blocks whose loads are in flight together
 // vk[j]) and the function returns true.
 template <bool L2>
 __device__ __forceinline__ bool act_rms_row(const float *xr, const float *rr, int64_t k, float eps, double *part,
-                                            float &scale, float (&vk)[kActBatch][8]) {
+                                            float &scale, float (&vk)[kActBatch][8], const ArRows *ar = nullptr) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nbk = int(k / kQK_K);
     const int nbw = nbk > warp ? (nbk - warp + 7) / 8 : 0;
@@ -142,7 +156,7 @@ __device__ __forceinline__ bool act_rms_row(const float *xr, const float *rr, in
     for (int j0 = 0; j0 < nbw; j0 += kActBatch) {
 #pragma unroll
         for (int jj = 0; jj < kActBatch; jj++)
-            if (j0 + jj < nbw) act_load_v<L2>(kActRms, xr, rr, warp + 8 * (j0 + jj), vk[jj]);
+            if (j0 + jj < nbw) act_load_v<L2>(kActRms, xr, rr, warp + 8 * (j0 + jj), vk[jj], ar);
 #pragma unroll
         for (int jj = 0; jj < kActBatch; jj++)
             if (j0 + jj < nbw) {
@@ -172,21 +186,36 @@ __global__ void __launch_bounds__(256) act_prep_kernel(const ActPrepArgs a) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ double part[8];
+    __shared__ unsigned ar_seq;
     const int warp = threadIdx.x >> 5;
     const int t = blockIdx.y;
     const int nbk = int(a.k / kQK_K);
     const float *xr = a.x + t * a.x_stride;
     const float *rr = a.r ? a.r + t * a.x_stride : nullptr;
+    ArRows rows;
+    const ArRows *arp = nullptr;
+    if (a.ar.on) {
+        // r = the sum over ranks of the all-reduced output (LL words, waited for one by one)
+        if (threadIdx.x == 0) ar_seq = ar_consumer_seq(a.ar);
+        __syncthreads();
+        const int par = int(ar_seq & 1u);
+        rows.n = a.ar.world;
+        rows.seq = ar_seq;
+        rows.p0 = a.ar.base + int64_t(par) * a.ar.world * a.ar.n_max + int64_t(t) * a.ar.n;
+        rows.stride = a.ar.n_max;
+        arp = &rows;
+    }
     float scale = 1.0f;
     if (a.mode == kActRms) {
         float vk[kActBatch][8];
-        act_rms_row<false>(xr, rr, a.k, a.eps, part, scale, vk);
+        act_rms_row<false>(xr, rr, a.k, a.eps, part, scale, vk, arp);
     }
     const int b = blockIdx.x * 8 + warp;
     if (b >= nbk) return;
     float v[8];
-    act_load_v<false>(a.mode, xr, rr, b, v);
-    if (a.mode == kActRms && rr && a.h_out) store8(a.h_out + t * a.x_stride + int64_t(b) * kQK_K + (threadIdx.x & 31) * 8, v);
+    act_load_v<false>(a.mode, xr, rr, b, v, arp);
+    if (a.mode == kActRms && (rr || arp) && a.h_out)
+        store8(a.h_out + t * a.x_stride + int64_t(b) * kQK_K + (threadIdx.x & 31) * 8, v);
     act_quantize_store(a.mode, v, scale, a.g, b, t, a.k, a.m, a.out);
 }
 

@@ -424,7 +424,8 @@ static cudaError_t launch_q4k_row_t(RowArgs &a, int smem, cudaStream_t st) {
 // M <= 3: the activation image is built by act_prep_kernel (with the fused
 // prologue), then the row GEMV pulls it in with one bulk copy.
 static cpq_status run_q4k_row(const GemvArgs &g, const float *x, int64_t x_stride, int m, const cpq_prologue &pro,
-                              uint8_t *ws, cudaStream_t st) {
+                              uint8_t *ws, cudaStream_t st, const ArIn *ar_in = nullptr,
+                              const ArOut *ar_out = nullptr) {
     static thread_local RowArgs a;
     std::memset(&a, 0, sizeof a);
     const int64_t k = g.k;
@@ -443,7 +444,7 @@ static cpq_status run_q4k_row(const GemvArgs &g, const float *x, int64_t x_strid
         return fail(CPQ_ERR_UNSUPPORTED, "too many row blocks (%lld) for the workspace counters",
                     (long long)a.mb_start[g.n_w]);
     uint8_t *act = ws + kWsActOffset;
-    ActPrepArgs pa;
+    ActPrepArgs pa = {};
     pa.mode = pro.mode;
     pa.x = x;
     pa.r = pro.r;
@@ -455,6 +456,10 @@ static cpq_status run_q4k_row(const GemvArgs &g, const float *x, int64_t x_strid
     pa.eps = pro.eps;
     pa.out = act;
     const int nbk = int(k / kQK_K);
+    if (ar_in) {
+        pa.ar = *ar_in;
+        pa.ar.n_ctas = unsigned((nbk + 7) / 8) * unsigned(m);  // act_prep_kernel's grid below
+    }
     cudaError_t e = launch(act_prep_kernel, dim3(unsigned((nbk + 7) / 8), unsigned(m)), dim3(256), 0, st, pa);
     if (e != cudaSuccess) return cuda_fail(e, "act_prep launch");
     a.nbk = nbk;
@@ -462,6 +467,7 @@ static cpq_status run_q4k_row(const GemvArgs &g, const float *x, int64_t x_strid
     a.act = act;
     a.partials = reinterpret_cast<float *>(ws + kWsCountersBytes);
     a.counters = reinterpret_cast<int *>(ws);
+    if (ar_out) a.ar = *ar_out;
     const int smem = row_smem_bytes(k, m);
     switch (m) {
     case 1: e = launch_q4k_row_t<1>(a, smem, st); break;
@@ -600,8 +606,13 @@ static cpq_status run_q4k_tc(const GemvArgs &g, const float *x, int64_t x_stride
 }
 
 // Quantize X once into the workspace, then run every weight against it.
+static ArOut ar_out_of(const cpq_tp_ar *ar, int64_t n);
+static ArIn ar_in_of(const cpq_tp_ar *ar, int64_t n);
+static bool ar_ready(const cpq_tp_ar *ar, int64_t need, const char **why);
+
 static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
-                               const cpq_prologue *pro_in, void *ws, size_t ws_bytes, cudaStream_t st) {
+                               const cpq_prologue *pro_in, void *ws, size_t ws_bytes, cudaStream_t st,
+                               const cpq_tp_ar *r_ar = nullptr, const cpq_tp_ar *y_ar = nullptr) {
     cpq_prologue pro = {CPQ_PRO_NONE, nullptr, nullptr, nullptr, 0.0f};
     if (pro_in) pro = *pro_in;
     if (pro.mode != CPQ_PRO_NONE && pro.mode != CPQ_PRO_RMS && pro.mode != CPQ_PRO_SWIGLU)
@@ -645,6 +656,27 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
     int64_t x_stride = int64_t(x->nb[1] / 4);
 
     cudaError_t e;
+    if (r_ar || y_ar) {
+        // the fused allreduce lives in the decode GEMV (row kernel + its act_prep)
+        if (!(s0.wtype == CPQ_TYPE_Q4_K && m <= kRowMaxTokens && row_smem_bytes(s0.k, int(m)) <= kSmemMax))
+            return fail(CPQ_ERR_UNSUPPORTED, "fused allreduce: Q4_K with M <= %d only", kRowMaxTokens);
+        const char *why = "";
+        ArIn ain;
+        ArOut aout;
+        if (r_ar) {
+            if (pro.mode != CPQ_PRO_RMS || pro.r)
+                return fail(CPQ_ERR_INVALID_ARG, "fused allreduce input: the prologue must be RMS with r = NULL");
+            if (!ar_ready(r_ar, m * s0.k, &why)) return fail(CPQ_ERR_INVALID_ARG, "fused allreduce input: %s", why);
+            ain = ar_in_of(r_ar, s0.k);
+        }
+        if (y_ar) {
+            if (n_w != 1) return fail(CPQ_ERR_INVALID_ARG, "fused allreduce output: one weight per call");
+            if (!ar_ready(y_ar, m * a.row_start[1], &why))
+                return fail(CPQ_ERR_INVALID_ARG, "fused allreduce output: %s", why);
+            aout = ar_out_of(y_ar, a.row_start[1]);
+        }
+        return run_q4k_row(a, xp, x_stride, int(m), pro, wsb, st, r_ar ? &ain : nullptr, y_ar ? &aout : nullptr);
+    }
     if (s0.wtype == CPQ_TYPE_Q4_K && m <= kRowMaxTokens && row_smem_bytes(s0.k, int(m)) <= kSmemMax)
         return run_q4k_row(a, xp, x_stride, int(m), pro, wsb, st);
 
@@ -803,6 +835,15 @@ cpq_status cpq_mul_mat_fused(const cpq_tensor *const *w, cpq_tensor *const *y, i
     cpq_status rc = workspace_of_current(&ws, &bytes);
     if (rc) return rc;
     return mul_mat_core(w, y, n_w, x, pro, ws, bytes, static_cast<cudaStream_t>(stream));
+}
+
+cpq_status cpq_mul_mat_fused_ar(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
+                                const cpq_prologue *pro, cpq_tp_ar *r_ar, cpq_tp_ar *y_ar, void *stream) {
+    void *ws;
+    size_t bytes;
+    cpq_status rc = workspace_of_current(&ws, &bytes);
+    if (rc) return rc;
+    return mul_mat_core(w, y, n_w, x, pro, ws, bytes, static_cast<cudaStream_t>(stream), r_ar, y_ar);
 }
 
 cpq_status cpq_quantize_act(int32_t wtype, const float *x, void *out, int64_t k, int64_t m, void *stream) {

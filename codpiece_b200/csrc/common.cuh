@@ -169,6 +169,106 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// ---- fused allreduce channel (include/cpq.h cpq_tp_ar) ----------------------
+//
+// LL protocol (the one NCCL's LL uses): every value crosses NVLink together
+// with its sequence number in one naturally aligned 64-bit word
+// (seq << 32 | fp32 bits), written with a single 64-bit store, so a reader
+// that sees the expected sequence number in a word also sees that word's
+// value: no fences, no flags, no counters on the producer side. Every rank's
+// receive buffer holds [2 parities][world][n_max] such words; sequence
+// number s uses parity s & 1.
+
+constexpr int kArMaxRanks = 8;
+
+// Producer side (row GEMV of a row-parallel projection).
+struct ArOut {
+    uint64_t *peer[kArMaxRanks];  // each rank's receive buffer (this rank's included)
+    const unsigned *seq;          // this rank's count of consumed all-reduces (local)
+    int64_t n_max;                // words per (parity, rank) slot
+    int64_t n;                    // output rows (token stride in a slot)
+    int world, rank;
+    int on;
+};
+
+// Consumer side (the prologue that reads the all-reduced residual). The
+// consumer kernel's CTAs each read seq, then the last of them (arrive
+// counter) advances it.
+struct ArIn {
+    const uint64_t *base;         // this rank's receive buffer
+    unsigned *seq;
+    unsigned *arrive;             // consumer CTAs that have read seq (local, zero between calls)
+    int64_t n_max, n;
+    int world;
+    unsigned n_ctas;              // CTAs of the consumer launch
+    int on;
+};
+
+// The ranks' words for one token's row (rank s at p0 + s * stride), read
+// and summed in rank order.
+struct ArRows {
+    const uint64_t *p0;
+    int64_t stride;
+    int n;
+    unsigned seq;
+};
+
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// The value of one LL word once it carries sequence number seq (bounded wait;
+// on give-up the device error word is set and 0 is returned).
+__device__ __forceinline__ float ar_word(const uint64_t *p, unsigned seq) {
+    uint64_t w = ld_relaxed_sys_u64(p);
+    if (unsigned(w >> 32) != seq) {
+        const uint64_t t0 = global_timer_ns();
+        for (uint32_t it = 1;; ++it) {
+            w = ld_relaxed_sys_u64(p);
+            if (unsigned(w >> 32) == seq) break;
+            if ((it & 63u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(&g_dev_error, kDevErrWaitTimeout);
+                return 0.0f;
+            }
+        }
+    }
+    return __uint_as_float(unsigned(w));
+}
+
+__device__ __forceinline__ void ld_relaxed_sys_v2u64(const uint64_t *p, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Eight consecutive LL words (16-byte aligned) of one rank: the loads are
+// issued together, then any word without the expected sequence number is
+// waited for on its own.
+__device__ __forceinline__ void ar_words8(const uint64_t *p, unsigned seq, float (&v)[8]) {
+    uint64_t w[8];
+#pragma unroll
+    for (int i = 0; i < 4; i++) ld_relaxed_sys_v2u64(p + 2 * i, w[2 * i], w[2 * i + 1]);
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+        v[i] = unsigned(w[i] >> 32) == seq ? __uint_as_float(unsigned(w[i])) : ar_word(p + i, seq);
+}
+
+// Thread 0 of every consumer CTA: this call's sequence number; the last CTA
+// to read it advances the rank's count for the next all-reduce.
+__device__ __forceinline__ unsigned ar_consumer_seq(const ArIn &ar) {
+    const unsigned s = *reinterpret_cast<volatile unsigned *>(ar.seq) + 1u;
+    __threadfence();
+    if (atomicAdd(ar.arrive, 1u) == ar.n_ctas - 1) {
+        *ar.arrive = 0u;
+        *reinterpret_cast<volatile unsigned *>(ar.seq) = s;
+    }
+    return s;
+}
+
 // ---- activation views ------------------------------------------------------
 
 // Quantized activations (structure of arrays) for M rows of K elements.

@@ -57,6 +57,7 @@ struct alignas(64) RowArgs {
     int64_t n_warps;
     float *partials;      // [warp][2 segments][256 floats]
     int *counters;        // [row block], zero between calls
+    ArOut ar;             // on: weight 0's output is all-reduced through this channel
 };
 
 // Lane = row: this lane's 144-byte superblock (h = header, qv = nibbles)
@@ -116,14 +117,36 @@ struct RowSeg {
     int *counters;         // [row block]
 };
 
+// The finished values of one 32-row block (lane = row): stored in Y, or,
+// for an all-reduced output (ar non-null, sequence number ar_e), written to
+// slot (ar_e & 1, rank) of every rank's receive buffer over NVLink as LL
+// words (ar_e << 32 | value), one 64-bit store each: nothing else to publish.
 template <int MT>
-__device__ __forceinline__ void row_segment_end(const RowSeg &sg, int64_t mb, int nbk, bool whole, float (&acc)[MT],
-                                                float *y, int64_t y_stride, int m, bool row_ok, int64_t row) {
-    const int lane = threadIdx.x & 31;
-    if (whole) {
+__device__ __forceinline__ void row_block_out(const float (&v)[MT], float *y, int64_t y_stride, int m, bool row_ok,
+                                              int64_t row, const ArOut *ar, unsigned ar_e) {
+    if (!ar) {
 #pragma unroll
         for (int t = 0; t < MT; t++)
-            if (t < m && row_ok) y[size_t(t) * y_stride + row] = acc[t];
+            if (t < m && row_ok) y[size_t(t) * y_stride + row] = v[t];
+        return;
+    }
+    const int64_t slot = (int64_t(ar_e & 1u) * ar->world + ar->rank) * ar->n_max;
+    for (int d = 0; d < ar->world; d++) {
+        uint64_t *dst = ar->peer[d] + slot;
+#pragma unroll
+        for (int t = 0; t < MT; t++)
+            if (t < m && row_ok)
+                st_relaxed_sys_u64(dst + int64_t(t) * ar->n + row, (uint64_t(ar_e) << 32) | __float_as_uint(v[t]));
+    }
+}
+
+template <int MT>
+__device__ __forceinline__ void row_segment_end(const RowSeg &sg, int64_t mb, int nbk, bool whole, float (&acc)[MT],
+                                                float *y, int64_t y_stride, int m, bool row_ok, int64_t row,
+                                                const ArOut *ar = nullptr, unsigned ar_e = 0u) {
+    const int lane = threadIdx.x & 31;
+    if (whole) {
+        row_block_out<MT>(acc, y, y_stride, m, row_ok, row, ar, ar_e);
         return;
     }
     const int64_t first = owner_warp(mb * nbk, sg.G, sg.T);
@@ -166,10 +189,8 @@ __device__ __forceinline__ void row_segment_end(const RowSeg &sg, int64_t mb, in
                 }
             }
         }
-#pragma unroll
-        for (int t = 0; t < MT; t++)
-            if (t < m && row_ok) y[size_t(t) * y_stride + row] = sum[t];
         if (lane == 0) sg.counters[mb] = 0;
+        row_block_out<MT>(sum, y, y_stride, m, row_ok, row, ar, ar_e);
     }
 }
 
@@ -239,6 +260,8 @@ __global__ void __launch_bounds__(kRowWarps * 32, 1) gemv_q4k_row_kernel(const _
     }
     pdl_launch_dependents();
     if (!active) return;
+    const ArOut *arp = a.ar.on ? &a.ar : nullptr;
+    const unsigned ar_e = a.ar.on ? *a.ar.seq + 1u : 0u;  // this call's sequence number
 
     float acc[MT];
 #pragma unroll
@@ -278,7 +301,7 @@ __global__ void __launch_bounds__(kRowWarps * 32, 1) gemv_q4k_row_kernel(const _
             const int64_t row0 = (c_mb - a.mb_start[wi]) * kRowRows;
             const bool row_ok = row0 + lane < a.n[wi];
             row_segment_end<MT>(sg, c_mb, nbk, seg_start == c_mb * nbk && blk_end, acc, a.y[wi], a.y_stride[wi], a.m,
-                                row_ok, row0 + lane);
+                                row_ok, row0 + lane, arp, ar_e);
 #pragma unroll
             for (int t = 0; t < MT; t++) acc[t] = 0.0f;
             seg_start = c_it;

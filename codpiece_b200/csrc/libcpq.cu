@@ -17,6 +17,7 @@
 //   api.inl          extern "C" entry points declared in include/cpq.h
 //   noalloc.inl      cpq_mul_mat_noalloc: decode GEMV on static device scratch
 //   plan.inl         cpq_decode_plan_*: host side of the persistent decode kernel
+//   tp_ar.inl        cpq_tp_ar_*: the fused allreduce channel over NVLink peer memory
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ < 1000
 #error "libcpq targets sm_100a (B200) only"
 #endif
@@ -42,3 +43,4 @@
 #include "api.inl"
 #include "noalloc.inl"
 #include "plan.inl"
+#include "tp_ar.inl"

@@ -120,7 +120,7 @@ extern "C" cpq_status cpq_mul_mat_noalloc(const cpq_tensor *w, const cpq_tensor 
 
     cudaError_t e = cudaMemsetAsync(counters, 0, kNoAllocCounterBytes, st);
     if (e != cudaSuccess) return cuda_fail(e, "cpq_mul_mat_noalloc: clearing the counters");
-    ActPrepArgs pa;
+    ActPrepArgs pa = {};
     pa.mode = kActPlain;
     pa.x = static_cast<const float *>(x->data);
     pa.r = nullptr;

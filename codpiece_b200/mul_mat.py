@@ -159,9 +159,14 @@ def _ptr(t):
 
 def mul_mat_fused(ws: list[QTensor], x: torch.Tensor, outs: list[torch.Tensor] | None = None, *, mode: int = PRO_NONE,
                   r: torch.Tensor | None = None, g: torch.Tensor | None = None, h_out: torch.Tensor | None = None,
-                  eps: float = 1e-6, stream=None) -> list[torch.Tensor]:
+                  eps: float = 1e-6, stream=None, r_ar: "ArChannel | None" = None,
+                  y_ar: "ArChannel | None" = None) -> list[torch.Tensor]:
     """Y_i = W_i x quantize(f(X)) with f the fused prologue (include/cpq.h cpq_prologue):
-    PRO_RMS: rms_norm(X + r) * g (X + r stored to h_out when given); PRO_SWIGLU: silu(X) * r."""
+    PRO_RMS: rms_norm(X + r) * g (X + r stored to h_out when given); PRO_SWIGLU: silu(X) * r.
+
+    With a fused-allreduce channel (cpq_mul_mat_fused_ar): y_ar all-reduces
+    Y_0 through the channel instead of storing it; r_ar makes the RMS
+    residual r the sum over ranks of the channel's last all-reduced value."""
     if x.dim() == 1:
         x = x.unsqueeze(0)
     if outs is None:
@@ -174,7 +179,13 @@ def mul_mat_fused(ws: list[QTensor], x: torch.Tensor, outs: list[torch.Tensor] |
     warr = (C.POINTER(CpqTensor) * n)(*[C.pointer(d) for d in wds])
     yarr = (C.POINTER(CpqTensor) * n)(*[C.pointer(d) for d in yds])
     pro = CpqPrologue(mode, _ptr(r), _ptr(g), _ptr(h_out), eps)
-    check(lib().cpq_mul_mat_fused(warr, yarr, n, C.byref(xd), C.byref(pro), _stream(stream)), "cpq_mul_mat_fused")
+    if r_ar is None and y_ar is None:
+        check(lib().cpq_mul_mat_fused(warr, yarr, n, C.byref(xd), C.byref(pro), _stream(stream)), "cpq_mul_mat_fused")
+    else:
+        check(lib().cpq_mul_mat_fused_ar(warr, yarr, n, C.byref(xd), C.byref(pro),
+                                         r_ar.handle if r_ar is not None else None,
+                                         y_ar.handle if y_ar is not None else None, _stream(stream)),
+              "cpq_mul_mat_fused_ar")
     return outs
 
 
@@ -289,6 +300,45 @@ class DecodePlan:
     def close(self) -> None:
         if self.handle:
             lib().cpq_decode_plan_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+class ArChannel:
+    """A fused-allreduce channel over NVLink peer memory (include/cpq.h cpq_tp_ar_*).
+
+    Create one per rank, exchange the 64-byte IPC handles (``handle``) in rank
+    order (e.g. torch.distributed.all_gather_object), then connect()."""
+
+    def __init__(self, world: int, rank: int, n_max: int, device: int | None = None):
+        dev = torch.cuda.current_device() if device is None else device
+        self.handle = C.c_void_p()
+        buf = C.create_string_buffer(64)
+        check(lib().cpq_tp_ar_create(dev, world, rank, n_max, C.byref(self.handle), buf), "cpq_tp_ar_create")
+        self.ipc_handle = buf.raw
+        self.world, self.rank = world, rank
+
+    def connect(self, handles: list[bytes]) -> None:
+        if len(handles) != self.world or any(len(h) != 64 for h in handles):
+            raise ValueError("one 64-byte handle per rank expected")
+        blob = C.create_string_buffer(b"".join(handles), 64 * self.world)
+        check(lib().cpq_tp_ar_connect(self.handle, blob), "cpq_tp_ar_connect")
+
+    def add(self, x: torch.Tensor, out: torch.Tensor, stream=None) -> torch.Tensor:
+        """out = x + the sum over ranks of the last value all-reduced through the channel."""
+        m, k = x.shape
+        check(lib().cpq_tp_ar_add(self.handle, C.c_void_p(x.data_ptr()), C.c_void_p(out.data_ptr()), k, m,
+                                  _stream(stream)), "cpq_tp_ar_add")
+        return out
+
+    def close(self) -> None:
+        if self.handle:
+            lib().cpq_tp_ar_destroy(self.handle)
             self.handle = C.c_void_p()
 
     def __del__(self):

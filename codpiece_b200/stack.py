@@ -84,7 +84,7 @@ class Stack:
 
     def __init__(self, hp: tp.Hparams, n_layer: int, rank: int = 0, world: int = 1, comm: Comm | None = None,
                  m: int = 1, seed: int = 0, head: bool = True, device: int | None = None, eps: float = 1e-6,
-                 use_plan: bool = False):
+                 use_plan: bool = False, ar_exchange=None):
         self.hp, self.n_layer, self.rank, self.world, self.comm, self.m = hp, n_layer, rank, world, comm, m
         self.eps = eps
         self.dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
@@ -130,6 +130,13 @@ class Stack:
         mm.init(self.dev.index, 64 << 20)
         self.graph: torch.cuda.CUDAGraph | None = None
         self.plan: mm.DecodePlan | None = None
+        # Row-parallel partial sums: through the fused NVLink allreduce when the
+        # caller supplies a handle exchange (decode M <= 3 with the head), else NCCL.
+        self.ar: mm.ArChannel | None = None
+        if ar_exchange is not None and world > 1 and m <= 3 and head and all(
+                lw.o is not None and lw.down is not None for lw in self.layers):
+            self.ar = mm.ArChannel(world, rank, m * e, self.dev.index)
+            self.ar.connect(list(ar_exchange(self.ar.ipc_handle)))
         if use_plan:
             if world != 1 or m != 1:
                 raise ValueError("decode plans run the single-GPU M = 1 step")
@@ -214,6 +221,7 @@ class Stack:
             self.plan.run()
             h, h_alt = self._plan_h
             part_live = len(self.layers) > 0
+        ch = self.ar
         for lw in ([] if self.plan is not None else self.layers):
             # attention block: xn = rms(h [+ part]) -> q, k, v
             ws, outs = [], []
@@ -222,7 +230,10 @@ class Stack:
                     ws.append(w)
                     outs.append(self._sl(b, w.n))
             if part_live:
-                if ws:
+                if ws and ch is not None:
+                    mm.mul_mat_fused(ws, h, outs, mode=mm.PRO_RMS, h_out=h_alt, eps=self.eps, r_ar=ch)
+                    h, h_alt = h_alt, h
+                elif ws:
                     mm.mul_mat_fused(ws, h, outs, mode=mm.PRO_RMS, r=self.part, h_out=h_alt, eps=self.eps)
                     h, h_alt = h_alt, h
                 else:
@@ -230,24 +241,36 @@ class Stack:
             elif ws:
                 mm.mul_mat_fused(ws, h, outs, mode=mm.PRO_RMS, eps=self.eps)
             # o projection (row-parallel)
-            if lw.o is not None:
+            if ch is not None:
+                mm.mul_mat_fused([lw.o], self._sl(self.qb, lw.o.k), [self.part], y_ar=ch)
+            elif lw.o is not None:
                 mm.mul_mat(lw.o, self._sl(self.qb, lw.o.k), out=self.part)
             else:
                 self.part.zero_()
-            if self.world > 1:
+            if self.world > 1 and ch is None:
                 self.comm.allreduce_(self.part)
             # ffn: xn = rms(h + part) -> gate, up ; h_alt = h + part
             nf = lw.gate.n
             g, u = self._sl(self.gb, nf), self._sl(self.ub, nf)
-            mm.mul_mat_fused([lw.gate, lw.up], h, [g, u], mode=mm.PRO_RMS, r=self.part, h_out=h_alt, eps=self.eps)
+            if ch is not None:
+                mm.mul_mat_fused([lw.gate, lw.up], h, [g, u], mode=mm.PRO_RMS, h_out=h_alt, eps=self.eps, r_ar=ch)
+            else:
+                mm.mul_mat_fused([lw.gate, lw.up], h, [g, u], mode=mm.PRO_RMS, r=self.part, h_out=h_alt,
+                                 eps=self.eps)
             h, h_alt = h_alt, h
             # down (row-parallel) with silu(gate) * up fused into its quantizer
-            mm.mul_mat_fused([lw.down], g, [self.part], mode=mm.PRO_SWIGLU, r=u)
-            if self.world > 1:
+            mm.mul_mat_fused([lw.down], g, [self.part], mode=mm.PRO_SWIGLU, r=u, y_ar=ch)
+            if self.world > 1 and ch is None:
                 self.comm.allreduce_(self.part)
             part_live = True
         if self.head is not None:
-            mm.mul_mat_fused([self.head], h, [self.logits], mode=mm.PRO_RMS, r=self.part, h_out=h_alt, eps=self.eps)
+            if ch is not None and part_live:
+                # the head is Q6_K: materialize h + allreduce(part) through a Q4_K-free path
+                self._head_prologue_ar(h, h_alt)
+                mm.mul_mat_fused([self.head], h_alt, [self.logits], mode=mm.PRO_RMS, eps=self.eps)
+            else:
+                mm.mul_mat_fused([self.head], h, [self.logits], mode=mm.PRO_RMS, r=self.part, h_out=h_alt,
+                                 eps=self.eps)
             h, h_alt = h_alt, h
             mm.argmax(self.logits, out=self.tok)
         elif part_live:
@@ -270,8 +293,15 @@ class Stack:
     def replay(self) -> None:
         self.graph.replay()
 
+    def _head_prologue_ar(self, h, h_out) -> None:
+        """h_out = h + allreduce(part) for the Q6_K head (outside the Q4_K decode GEMV)."""
+        self.ar.add(h, h_out)
+
     def release(self) -> None:
         self.graph = None
+        if self.ar is not None:
+            self.ar.close()
+            self.ar = None
         if self.plan is not None:
             self.plan.close()
             self.plan = None

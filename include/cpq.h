@@ -255,6 +255,53 @@ cpq_status cpq_tp_comm_check(cpq_comm *comm);
 /* Destroys (or, with abort != 0, aborts) the communicator. */
 cpq_status cpq_tp_comm_destroy(cpq_comm *comm, int abort);
 
+/* ---- fused allreduce over NVLink peer memory --------------------------------
+ *
+ * For the row-parallel projections (attn_output, ffn_down) of the decode
+ * step (M <= 3): the GEMV's row-block finalizers store their fp32 partial
+ * sums straight into every rank's receive buffer (P2P stores over NVLink,
+ * buffers shared through CUDA IPC), and the next fused call's RMS prologue
+ * sums the ranks' partials (in rank order) while it reads its residual
+ * input. This replaces cpq_tp_allreduce_f32 on the decode path. No reference
+ * counterpart: codpiece sums these partials with ggml's meta-backend
+ * allreduce (split.rs PARTIAL outputs, meta.rs).
+ *
+ * Protocol (LL, as in NCCL's LL): each value travels with the all-reduce's
+ * sequence number s in one 64-bit word written by a single store, so a
+ * reader that sees s in a word also sees its value; nothing else is
+ * published. All ranks run the same sequence of all-reduces; s alternates
+ * between two buffer halves (s & 1), and a rank cannot produce s + 2 before
+ * every rank has consumed s. A consumer waits for each word at most 2 s
+ * (then the device error word is set).
+ */
+typedef struct cpq_tp_ar cpq_tp_ar;
+
+/* Allocates this rank's receive buffer (n_max floats per rank and parity,
+ * n_max >= M * N of the projections) on `device` and writes its CUDA IPC
+ * handle (64 bytes) to handle64. world <= 8. */
+cpq_status cpq_tp_ar_create(int device, int world, int rank, int64_t n_max, cpq_tp_ar **ar, void *handle64);
+/* Opens the other ranks' buffers from world x 64 bytes of handles in rank order. */
+cpq_status cpq_tp_ar_connect(cpq_tp_ar *ar, const void *handles);
+/* Closes the peers' mappings and frees the buffer (all ranks' calls must
+ * have completed). NULL is ignored. */
+void cpq_tp_ar_destroy(cpq_tp_ar *ar);
+
+/* out = x + the sum over ranks of the channel's last all-reduced value, m
+ * rows of k floats (waits, bounded, for every rank's partial). For the
+ * consumers outside the Q4_K decode GEMV (e.g. the Q6_K LM head's residual). */
+cpq_status cpq_tp_ar_add(cpq_tp_ar *ar, const float *x, float *out, int64_t k, int64_t m, void *stream);
+
+/* cpq_mul_mat_fused with a channel at either end (either may be NULL):
+ *  y_ar  Y_0 (n_w must be 1) is all-reduced through the channel instead of
+ *        being stored in y[0] (y[0] still gives the shape);
+ *  r_ar  the RMS prologue's residual r is the sum over ranks of the last
+ *        value all-reduced through the channel (pro->mode CPQ_PRO_RMS,
+ *        pro->r NULL, h_out as usual).
+ * Q4_K weights and M <= 3 (the decode GEMV) only; anything else returns
+ * CPQ_ERR_UNSUPPORTED. */
+cpq_status cpq_mul_mat_fused_ar(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
+                                const cpq_prologue *pro, cpq_tp_ar *r_ar, cpq_tp_ar *y_ar, void *stream);
+
 /* ---- synthetic weights ----------------------------------------------------- */
 
 /* Fills rows [row0, row0+n_rows) x blocks [blk0, blk0+n_blk) of a tensor of

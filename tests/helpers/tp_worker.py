@@ -25,6 +25,7 @@ def main() -> int:
     out_path = sys.argv[1]
     layers = int(sys.argv[2]) if len(sys.argv) > 2 else 2
     m = int(sys.argv[3]) if len(sys.argv) > 3 else 1
+    fused_ar = len(sys.argv) > 4 and sys.argv[4] == "ar"
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
@@ -35,10 +36,28 @@ def main() -> int:
     dist.broadcast_object_list(obj, src=0)
     comm = st.Comm(world, rank, obj[0], local, timeout_ms=60000)
     h0 = torch.randn(m, 5120, generator=torch.Generator().manual_seed(11)) * 2
-    s = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=5)
+    def exchange(handle: bytes) -> list:
+        got = [None] * world
+        dist.all_gather_object(got, handle)
+        return got
+
+    s = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=5, ar_exchange=exchange if fused_ar else None)
+    assert (s.ar is not None) == fused_ar
     s.h.copy_(h0)
     s.step_body()
     torch.cuda.synchronize()
+    if fused_ar:  # a second step and a captured replay must agree with the first
+        first = (s.h_final.clone(), s.logits.clone())
+        s.h.copy_(h0)
+        s.step_body()
+        s.h.copy_(h0)
+        s.capture()
+        s.h.copy_(h0)
+        s.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(first[0], s.h_final) and torch.equal(first[1], s.logits)
+        from codpiece_b200 import mul_mat as mm
+        assert mm.device_status(local) == 0
     logits_tp = s.logits.cpu().numpy()
     h_tp = s.h_final.cpu().numpy()
     tok_tp = s.tok.cpu().numpy()
@@ -53,13 +72,15 @@ def main() -> int:
         torch.cuda.synchronize()
         lr, hr = ref.logits.cpu().numpy(), ref.h_final.cpu().numpy()
         verdict = {
-            "world": world, "layers": layers, "m": m,
+            "world": world, "layers": layers, "m": m, "fused_ar": fused_ar,
             "logits_rel": float(np.abs(logits_tp - lr).max() / np.abs(lr).max()),
             "h_rel": float(np.abs(h_tp - hr).max() / np.abs(hr).max()),
             "tok_tp": tok_tp.tolist(), "tok_ref": ref.tok.cpu().numpy().tolist(),
             "ranks_agree": all(g == gathered[0] for g in gathered),
         }
         comm.check()
+    dist.barrier(device_ids=[local])
+    s.release()
     dist.barrier(device_ids=[local])
     comm.destroy()
     dist.destroy_process_group()

@@ -32,18 +32,22 @@ def _ngpus():
     return torch.cuda.device_count()
 
 
-@pytest.mark.parametrize("world,layers,m", [(2, 2, 1), (2, 2, 8), (4, 2, 1), (8, 2, 1)])
-def test_tensor_parallel_stack_matches_tp1(cuda, tmp_path, world, layers, m):
+@pytest.mark.parametrize("world,layers,m,mode", [(2, 2, 1, "nccl"), (2, 2, 8, "nccl"), (2, 3, 1, "ar"), (2, 2, 3, "ar"),
+                                                 (4, 2, 1, "ar"), (8, 2, 1, "ar"), (8, 2, 8, "nccl")])
+def test_tensor_parallel_stack_matches_tp1(cuda, tmp_path, world, layers, m, mode):
+    """mode "ar": the row-parallel partial sums go through the fused NVLink allreduce
+    (cpq_mul_mat_fused_ar); "nccl": through cpq_tp_allreduce_f32."""
     if _ngpus() < world:
         pytest.skip(f"needs {world} GPUs")
     out = tmp_path / "verdict.json"
     env = dict(os.environ, NCCL_DEBUG="WARN")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
-           str(ROOT / "tests" / "helpers" / "tp_worker.py"), str(out), str(layers), str(m)]
+           str(ROOT / "tests" / "helpers" / "tp_worker.py"), str(out), str(layers), str(m), mode]
     res = subprocess.run(cmd, cwd=str(ROOT), env=env, capture_output=True, text=True)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     v = json.loads(out.read_text())
+    assert v["fused_ar"] == (mode == "ar")
     assert v["ranks_agree"]
     assert v["logits_rel"] <= TOL and v["h_rel"] <= TOL, v
     assert v["tok_tp"] == v["tok_ref"], v
