@@ -178,7 +178,7 @@ __device__ __forceinline__ bool act_rms_row(const float *xr, const float *rr, in
 }
 
 // grid: (ceil(nbk / 8), m); block 256 = 8 warps, warp w quantizes block 8*blockIdx.x + w of token blockIdx.y
-__global__ void __launch_bounds__(256) act_prep_kernel(const ActPrepArgs a) {
+__global__ void __launch_bounds__(256, 1) act_prep_kernel(const ActPrepArgs a) {
     // Dependents (the row GEMV) may launch before this kernel even starts
     // waiting: they only prefetch weights until their own griddepcontrol.wait,
     // which still orders them after this kernel, and so they take each SM as

@@ -224,7 +224,9 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *p) {
 }
 
 // The value of one LL word once it carries sequence number seq (bounded wait;
-// on give-up the device error word is set and 0 is returned).
+// on give-up the device error word is set and 0 is returned). Once any wait
+// on this device has given up, later words are not waited for at all, so a
+// broken peer costs one timeout, not one per word.
 __device__ __forceinline__ float ar_word(const uint64_t *p, unsigned seq) {
     uint64_t w = ld_relaxed_sys_u64(p);
     if (unsigned(w >> 32) != seq) {
@@ -232,7 +234,8 @@ __device__ __forceinline__ float ar_word(const uint64_t *p, unsigned seq) {
         for (uint32_t it = 1;; ++it) {
             w = ld_relaxed_sys_u64(p);
             if (unsigned(w >> 32) == seq) break;
-            if ((it & 63u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+            if ((it & 63u) == 0 && ((*reinterpret_cast<volatile uint32_t *>(&g_dev_error) & kDevErrWaitTimeout) ||
+                                    global_timer_ns() - t0 > kWaitLimitNs)) {
                 atomicOr(&g_dev_error, kDevErrWaitTimeout);
                 return 0.0f;
             }
