@@ -593,13 +593,17 @@ static cpq_status run_q4k_tc(const GemvArgs &g, const float *x, int64_t x_stride
         const int64_t n = g.row_start[i + 1] - g.row_start[i];
         if (n == 0) continue;
         const int64_t pairs = (n + 2 * kTcRows - 1) / (2 * kTcRows);
-        if (pairs > 65535) return fail(CPQ_ERR_UNSUPPORTED, "N=%lld rows is too many for one call", (long long)n);
+        if (pairs > (int64_t(1) << 30) / n_tok_tiles)
+            return fail(CPQ_ERR_UNSUPPORTED, "N=%lld rows is too many for one call", (long long)n);
         if ((rc = q4k_tensor_map(g.w[i], n, k, g.rs, &a.tmap_w, kTcRows, 1))) return rc;
         a.y = g.y[i];
         a.y_stride = g.y_stride[i];
         a.n = n;
-        e = launch_pair(gemm_q4k_tc_kernel, dim3(2, unsigned(n_tok_tiles), unsigned(pairs)), dim3(kTcThreads),
-                        size_t(kTcSmem), st, a);
+        a.n_pairs = int(pairs);
+        a.n_tok_tiles = int(n_tok_tiles);
+        // persistent: one CTA pair per two SMs (at most one per tile)
+        const int64_t grid_pairs = std::min<int64_t>(sm_count(dev) / 2, pairs * n_tok_tiles);
+        e = launch_pair(gemm_q4k_tc_kernel, dim3(unsigned(2 * grid_pairs)), dim3(kTcThreads), size_t(kTcSmem), st, a);
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core gemm launch");
     }
     return CPQ_SUCCESS;

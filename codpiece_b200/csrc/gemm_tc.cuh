@@ -89,7 +89,7 @@ constexpr int kTcBAtomBytes = kTcMaxTok / 2 * 128;  // one swizzle atom column o
 constexpr int kTcBBytes = kTcBAtomBytes * (kTcK / kTcAtomK);
 constexpr int kTcRawBytes = kTcRows * kQ4K_Bytes;
 constexpr int kTcBarOffset = kTcBStages * kTcBBytes + kTcRawSlots * kTcRawBytes;
-constexpr int kTcBarBytes = int(align_up((2 * (kTcAStages + kTcBStages + kTcRawSlots) + 1) * 8 + 8, 128));
+constexpr int kTcBarBytes = int(align_up((2 * (kTcAStages + kTcBStages + kTcRawSlots) + 2) * 8 + 8, 128));
 constexpr int kTcSmem = kTcBarOffset + kTcBarBytes /* barriers, TMEM slot, abort flag */ + 1024 /* alignment slack */;
 static_assert(kTcRawBytes % 1024 == 0 && kTcBBytes % 1024 == 0, "1024-byte stage bases");
 static_assert(kTcSmem <= 227 * 1024, "shared memory");
@@ -103,6 +103,8 @@ struct alignas(64) TcArgs {
     int64_t m;           // tokens
     int nbk;             // superblocks per row
     int tile_n;          // tokens per pair tile (multiple of 32, 32..256)
+    int n_pairs;         // 256-row tiles (row pairs)
+    int n_tok_tiles;     // token tiles
 };
 
 // ---- tcgen05 / descriptor helpers ------------------------------------------
@@ -253,8 +255,14 @@ __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<co
 
 // ---- the kernel -------------------------------------------------------------
 
-// grid: (2, token tiles, row-pair tiles), cluster (2, 1, 1) — the token tiles
-// of one weight tile run side by side, so its raw bytes come from HBM about once.
+// Persistent: grid = 2 x (number of CTA pairs), cluster (2, 1, 1). Pair c
+// runs tiles c, c + pairs, ... of the (row pair, token tile) space, token
+// tile fastest, so the token tiles of one weight tile run close together and
+// its raw bytes come from HBM about once. Stage, slot and parity counters run
+// across tiles, so the producers stream straight into the next tile; the
+// accumulator is handed between the MMA issuer and the epilogue with
+// acc_full (multicast commit) and acc_empty (8 epilogue warps of each CTA
+// arrive on rank 0).
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid_constant__ TcArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -263,16 +271,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kTcBarOffset);
     uint64_t *fullA = bars, *emptyA = fullA + kTcAStages;
     uint64_t *fullB = emptyA + kTcAStages, *emptyB = fullB + kTcBStages;
-    uint64_t *rawFull = emptyB + kTcBStages, *rawEmpty = rawFull + kTcRawSlots, *done = rawEmpty + kTcRawSlots;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    uint64_t *rawFull = emptyB + kTcBStages, *rawEmpty = rawFull + kTcRawSlots;
+    uint64_t *acc_full = rawEmpty + kTcRawSlots, *acc_empty = acc_full + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
     const int tile_n = a.tile_n, half_n = tile_n / 2;
-    const int64_t tok0 = int64_t(blockIdx.y) * tile_n;
-    const int64_t row0 = int64_t(blockIdx.z) * (2 * kTcRows) + int64_t(rank) * kTcRows;
-    const int nk = a.nbk * (kQK_K / kTcK);
+    const int nk = a.nbk * (kQK_K / kTcK);        // stages per tile
+    const int64_t n_tiles = int64_t(a.n_pairs) * a.n_tok_tiles;
+    const int64_t pair = blockIdx.x >> 1, n_pairs_grid = gridDim.x >> 1;
+    // this pair's i-th tile: row pair and token tile
+    auto tile_rows = [&](int64_t tile) { return (tile / a.n_tok_tiles) * (2 * kTcRows) + int64_t(rank) * kTcRows; };
+    auto tile_tok = [&](int64_t tile) { return (tile % a.n_tok_tiles) * tile_n; };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcAStages; s++) {
@@ -287,7 +299,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
             mbar_init(&rawFull[s], 1);
             mbar_init(&rawEmpty[s], kTcDqWarps);
         }
-        mbar_init(done, 1);
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 2 * kTcDqWarps);  // rank 0: every epilogue warp of both CTAs
         // a wait on this device has already timed out: do no work (the error stays reported)
         *abort_flag = (*reinterpret_cast<volatile uint32_t *>(&g_dev_error) & kDevErrWaitTimeout) ? 1 : 0;
         fence_mbar_init();
@@ -310,78 +323,115 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
         // ---- MMA issue (rank 0) ----
         if (rank == 0 && lane == 0) {
             const uint32_t idesc = tc_idesc_f16(2 * kTcRows, tile_n);
-            for (int t = 0; t < nk; t++) {
-                const int sa = t % kTcAStages, sb = t % kTcBStages;
-                if (!tc_wait(&fullA[sa], uint32_t(t / kTcAStages) & 1u, abort_flag) ||
-                    !tc_wait(&fullB[sb], uint32_t(t / kTcBStages) & 1u, abort_flag))
-                    break;
+            int64_t g = 0;      // stages issued so far (all tiles)
+            int it = 0;         // tiles of this pair so far
+            int committed = 0;  // acc_full commits issued
+            bool ok = true;
+            for (int64_t tile = pair; tile < n_tiles && ok; tile += n_pairs_grid, it++) {
+                // the epilogue has drained the previous tile's accumulator
+                if (it > 0 && !tc_wait(acc_empty, uint32_t(it - 1) & 1u, abort_flag)) break;
                 tc_fence_after();
-                const uint32_t at = tmem + kTcAccCols + kTcAStageCols * uint32_t(sa);
-                const uint64_t bd0 = smem_desc_sw128(smem_addr(sB + sb * kTcBBytes));
-                const uint64_t bd1 = smem_desc_sw128(smem_addr(sB + sb * kTcBBytes + kTcBAtomBytes));
+                for (int t = 0; t < nk; t++, g++) {
+                    const int sa = int(g % kTcAStages), sb = int(g % kTcBStages);
+                    if (!tc_wait(&fullA[sa], uint32_t(g / kTcAStages) & 1u, abort_flag) ||
+                        !tc_wait(&fullB[sb], uint32_t(g / kTcBStages) & 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t at = tmem + kTcAccCols + kTcAStageCols * uint32_t(sa);
+                    const uint64_t bd0 = smem_desc_sw128(smem_addr(sB + sb * kTcBBytes));
+                    const uint64_t bd1 = smem_desc_sw128(smem_addr(sB + sb * kTcBBytes + kTcBAtomBytes));
 #pragma unroll
-                for (int kk = 0; kk < kTcK / 16; kk++)  // K=16 per MMA: 8 TMEM columns of A, 32 bytes of a B atom (+2)
-                    tc_mma2_f16_ts(tmem, at + 8u * uint32_t(kk), (kk < 4 ? bd0 : bd1) + 2 * (kk & 3), idesc,
-                                   (t | kk) != 0 ? 1u : 0u);
-                tc_commit2(&emptyA[sa]);
-                tc_commit2(&emptyB[sb]);
+                    for (int kk = 0; kk < kTcK / 16; kk++)  // K=16 per MMA: 8 TMEM columns of A, 32 B of a B atom
+                        tc_mma2_f16_ts(tmem, at + 8u * uint32_t(kk), (kk < 4 ? bd0 : bd1) + 2 * (kk & 3), idesc,
+                                       (t | kk) != 0 ? 1u : 0u);
+                    tc_commit2(&emptyA[sa]);
+                    tc_commit2(&emptyB[sb]);
+                }
+                if (!ok) break;
+                tc_commit2(acc_full);
+                committed++;
             }
-            tc_commit2(done);
-            mbar_wait_bounded(done, 0);  // the accumulators are final (or idle) before TMEM is released
+            // every MMA issued has completed before TMEM is released: after an early stop, one
+            // more commit tracks the partly issued tile
+            if (!ok) {
+                tc_commit2(acc_full);
+                committed++;
+            }
+            if (committed > 0) mbar_wait_bounded(acc_full, uint32_t(committed - 1) & 1u);
         }
         __syncwarp();
     } else if (warp == 1) {
         // ---- this CTA's half of the activation stages (TMA, completing on rank 0) ----
         if (lane == 0) {
-            int t = 0;
-            for (; t < nk; t++) {
-                const int s = t % kTcBStages;
-                const uint32_t ph = uint32_t(t / kTcBStages) & 1u;
-                if (*abort_flag || !tc_wait(&emptyB[s], ph ^ 1u, abort_flag)) break;
-                if (rank == 0) mbar_arrive_expect_tx(&fullB[s], uint32_t(tile_n) * 2u * kTcK);
-                const uint32_t bar0 = cluster_addr(&fullB[s], 0);
+            int64_t g = 0;
+            bool ok = true;
+            for (int64_t tile = pair; tile < n_tiles && ok; tile += n_pairs_grid) {
+                const int tok = int(tile_tok(tile)) + int(rank) * half_n;
+                for (int t = 0; t < nk; t++, g++) {
+                    const int s = int(g % kTcBStages);
+                    const uint32_t ph = uint32_t(g / kTcBStages) & 1u;
+                    if (*abort_flag || !tc_wait(&emptyB[s], ph ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    if (rank == 0) mbar_arrive_expect_tx(&fullB[s], uint32_t(tile_n) * 2u * kTcK);
+                    const uint32_t bar0 = cluster_addr(&fullB[s], 0);
 #pragma unroll
-                for (int at = 0; at < kTcK / kTcAtomK; at++)
-                    tma_load_2d_pair(sB + s * kTcBBytes + at * kTcBAtomBytes, &a.tmap_x, t * kTcK + at * kTcAtomK,
-                                     int(tok0) + int(rank) * half_n, bar0);
+                    for (int q = 0; q < kTcK / kTcAtomK; q++)
+                        tma_load_2d_pair(sB + s * kTcBBytes + q * kTcBAtomBytes, &a.tmap_x, t * kTcK + q * kTcAtomK,
+                                         tok, bar0);
+                }
             }
             // no copy may land after the CTAs have exited: rank 0 waits for the last stages issued
             // (their barriers count both halves)
             if (rank == 0)
-                for (int u = t > kTcBStages ? t - kTcBStages : 0; u < t; u++)
+                for (int64_t u = g > kTcBStages ? g - kTcBStages : 0; u < g; u++)
                     mbar_wait_bounded(&fullB[u % kTcBStages], uint32_t(u / kTcBStages) & 1u);
         }
         __syncwarp();
     } else if (warp == 2) {
         // ---- raw Q4_K superblocks (TMA) ----
         if (lane == 0) {
-            int kb = 0;
-            for (; kb < a.nbk; kb++) {
-                const int s = kb % kTcRawSlots;
-                const uint32_t ph = uint32_t(kb / kTcRawSlots) & 1u;
-                if (*abort_flag || !tc_wait(&rawEmpty[s], ph ^ 1u, abort_flag)) break;
-                mbar_arrive_expect_tx(&rawFull[s], uint32_t(kTcRawBytes));
-                tma_load_2d(sRaw + s * kTcRawBytes, &a.tmap_w, kb * (kQ4K_Bytes / 8), int(row0), &rawFull[s]);
+            int64_t g = 0;
+            bool ok = true;
+            for (int64_t tile = pair; tile < n_tiles && ok; tile += n_pairs_grid) {
+                const int row0 = int(tile_rows(tile));
+                for (int kb = 0; kb < a.nbk; kb++, g++) {
+                    const int s = int(g % kTcRawSlots);
+                    const uint32_t ph = uint32_t(g / kTcRawSlots) & 1u;
+                    if (*abort_flag || !tc_wait(&rawEmpty[s], ph ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&rawFull[s], uint32_t(kTcRawBytes));
+                    tma_load_2d(sRaw + s * kTcRawBytes, &a.tmap_w, kb * (kQ4K_Bytes / 8), row0, &rawFull[s]);
+                }
             }
-            for (int u = kb > kTcRawSlots ? kb - kTcRawSlots : 0; u < kb; u++)
+            for (int64_t u = g > kTcRawSlots ? g - kTcRawSlots : 0; u < g; u++)
                 mbar_wait_bounded(&rawFull[u % kTcRawSlots], uint32_t(u / kTcRawSlots) & 1u);
         }
         __syncwarp();
     } else if (warp >= 4) {
-        // ---- dequantization (rows past n arrive zero-filled, so they dequantize to 0) ----
+        // ---- dequantization + epilogue (rows past n arrive zero-filled, so they dequantize to 0) ----
         const int dq = warp - 4;
         const int grp = dq >> 2;                      // superblock half (= stage parity) of this warp
         const int quarter = warp & 3;                 // TMEM lane quarter this warp may access
         const int r = 32 * quarter + lane;            // tile row = TMEM lane
         const uint32_t lane_base = uint32_t(32 * quarter) << 16;
+        const uint32_t acc_empty0 = cluster_addr(acc_empty, 0);
+        int64_t gs = 0;   // stages of all tiles so far (this warp handles those with gs % 2 == grp)
+        int64_t gr = 0;   // superblocks of all tiles so far
         bool ok = true;
-        for (int t = grp; t < nk; t += 2) {
-            const int sa = t % kTcAStages;
-            const uint32_t pa = uint32_t(t / kTcAStages) & 1u;
-            const int kb = t >> 1;
-            const int rs = kb % kTcRawSlots;
-            ok = __all_sync(0xffffffffu, tc_wait(&rawFull[rs], uint32_t(kb / kTcRawSlots) & 1u, abort_flag));
-            if (!ok) break;
+
+        // One stage: dequantize superblock half grp of stage t into A slot gs % kTcAStages.
+        auto dequant_stage = [&](int64_t g_stage, int64_t g_sb) -> bool {
+            const int sa = int(g_stage % kTcAStages);
+            const uint32_t pa = uint32_t(g_stage / kTcAStages) & 1u;
+            const int rs = int(g_sb % kTcRawSlots);
+            if (!__all_sync(0xffffffffu, tc_wait(&rawFull[rs], uint32_t(g_sb / kTcRawSlots) & 1u, abort_flag)))
+                return false;
             const uint8_t *raw = sRaw + rs * kTcRawBytes + r * kQ4K_Bytes;
             const uint4 hd = *reinterpret_cast<const uint4 *>(raw);
             uint4 qv[4];
@@ -394,8 +444,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
             const uint32_t mnw =
                 grp == 0 ? (hd.z & 0x3f3f3f3fu) : (((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u));
             const float d = half_bits_to_float(hd.x), dmin = half_bits_to_float(hd.x >> 16);
-            ok = __all_sync(0xffffffffu, tc_wait(&emptyA[sa], pa ^ 1u, abort_flag));
-            if (!ok) break;
+            if (!__all_sync(0xffffffffu, tc_wait(&emptyA[sa], pa ^ 1u, abort_flag))) return false;
             tc_fence_after();  // the MMAs that read this A stage have completed
 #pragma unroll
             for (int p = 0; p < 2; p++) {
@@ -426,13 +475,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(cluster_addr(&fullA[sa], 0));
-        }
+            return true;
+        };
 
-        // ---- epilogue: TMEM lane = tile row, column = token ----
-        if (ok) ok = __all_sync(0xffffffffu, tc_wait(done, 0, abort_flag));
-        if (ok) {
+        // The accumulator of tile `tile` (this pair's it-th) to Y, then released to the MMA issuer.
+        auto epilogue = [&](int64_t tile, int it) -> bool {
+            if (!__all_sync(0xffffffffu, tc_wait(acc_full, uint32_t(it) & 1u, abort_flag))) return false;
             tc_fence_after();
-            const int64_t orow = row0 + r;
+            const int64_t tok0 = tile_tok(tile);
+            const int64_t orow = tile_rows(tile) + r;
             const int64_t tend = a.m < tok0 + tile_n ? a.m : tok0 + tile_n;
             const int half = (((tile_n + 1) / 2) + 31) & ~31;
             const int cbeg = grp * half, cend = grp ? tile_n : (half < tile_n ? half : tile_n);
@@ -446,7 +497,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
                         if (tok0 + c0 + i < tend) yp[int64_t(i) * a.y_stride] = v[i];
                 }
             }
+            tc_fence_before();  // the TMEM reads are complete (tmem_ld32 waits for them)
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(acc_empty0);
+            return true;
+        };
+
+        int it = 0;
+        int64_t prev_tile = -1;
+        for (int64_t tile = pair; tile < n_tiles && ok; tile += n_pairs_grid, it++) {
+            // the first stages of this tile fill the A ring while the MMA finishes the previous
+            // tile; then this warp drains the previous tile's accumulator, then continues
+            const int64_t g0 = gs, r0 = gr;
+            int t = grp;
+            const int prefill = kTcAStages;  // stages of this tile (both groups) before the epilogue
+            for (; t < nk && t < prefill && ok; t += 2) ok = dequant_stage(g0 + t, r0 + (t >> 1));
+            if (ok && prev_tile >= 0) ok = epilogue(prev_tile, it - 1);
+            for (; t < nk && ok; t += 2) ok = dequant_stage(g0 + t, r0 + (t >> 1));
+            gs += nk;
+            gr += a.nbk;
+            prev_tile = tile;
         }
+        if (ok && prev_tile >= 0) epilogue(prev_tile, it - 1);
     }
 
     tc_fence_before();

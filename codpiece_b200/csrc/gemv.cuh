@@ -31,6 +31,9 @@ namespace cpq {
 #ifndef CPQ_Q4K_STAGES
 #define CPQ_Q4K_STAGES 6
 #endif
+#ifndef CPQ_Q6K_STAGES
+#define CPQ_Q6K_STAGES 4
+#endif
 
 constexpr int kGemvWarps = CPQ_GEMV_WARPS;  // warps per CTA
 constexpr int kMaxMulti = 4;   // weights sharing one activation in one launch
@@ -116,7 +119,7 @@ struct FmtQ6K {
     static constexpr int kBlkBytes = kQ6K_Bytes, kBlkElems = kQK_K;
     static constexpr int kCB = 8;  // 4 lanes per block
     static constexpr int kStageBytes = kCB * kBlkBytes + 32;  // 210 B blocks: up to 15 B misalignment
-    static constexpr int kStages = 4;
+    static constexpr int kStages = CPQ_Q6K_STAGES;
     static constexpr bool kAligned = false;
 
     template <int MT>
