@@ -104,3 +104,28 @@ def test_quantize_act_rejects_bad_shapes(L):
     assert L.cpq_quantize_act(12, None, None, 100, 1, None) == 1   # K not a multiple of 256
     assert L.cpq_quantize_act(30, None, None, 256, 1, None) == 2   # BF16 has no vec_dot_type here
     assert L.cpq_quantize_act(12, None, None, 256, 0, None) == 0   # empty
+
+
+def test_plan_and_channel_arguments_are_validated_on_the_host(L):
+    """cpq_decode_plan_create / cpq_tp_ar_create / cpq_tp_ar_add reject bad arguments before any device call."""
+    from codpiece_b200 import _lib
+    plan = C.c_void_p()
+    assert L.cpq_decode_plan_create(None, 1, 0, C.byref(plan)) == 1          # no phases
+    assert L.cpq_decode_plan_create((_lib.CpqDecodePhase * 1)(), 0, 0, C.byref(plan)) == 1
+    assert L.cpq_decode_plan_create((_lib.CpqDecodePhase * 1)(), 1, 0, None) == 1
+    ph = (_lib.CpqDecodePhase * 1)()
+    ph[0].mode, ph[0].n_w = 7, 1                                                # bad prologue mode
+    assert L.cpq_decode_plan_create(ph, 1, 0, C.byref(plan)) == 1
+    ph[0].mode, ph[0].n_w = 0, 4                                                # too many weights
+    assert L.cpq_decode_plan_create(ph, 1, 0, C.byref(plan)) == 1
+    assert b"n_w" in L.cpq_last_error()
+    L.cpq_decode_plan_destroy(None)                                             # NULL is ignored
+    ar = C.c_void_p()
+    h = C.create_string_buffer(64)
+    assert L.cpq_tp_ar_create(0, 9, 0, 5120, C.byref(ar), h) == 1              # world > 8
+    assert L.cpq_tp_ar_create(0, 2, 2, 5120, C.byref(ar), h) == 1              # rank out of range
+    assert L.cpq_tp_ar_create(0, 2, 0, 0, C.byref(ar), h) == 1                 # n_max
+    assert L.cpq_tp_ar_create(0, 2, 0, 5120, None, h) == 1
+    assert L.cpq_tp_ar_connect(None, h) == 1
+    assert L.cpq_tp_ar_add(None, None, None, 8, 1, None) == 1
+    L.cpq_tp_ar_destroy(None)
