@@ -213,8 +213,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+// 32 consecutive 32-bit TMEM columns of this thread's lane, without waiting
+// for the store to complete (tcgen05.wait::st does).
+__device__ __forceinline__ void tmem_st32_async(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%"
         "18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
@@ -223,8 +224,9 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
         "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Bounded wait that also gives up as soon as another role of the CTA aborted.
 __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
@@ -446,6 +448,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
             const float d = half_bits_to_float(hd.x), dmin = half_bits_to_float(hd.x >> 16);
             if (!__all_sync(0xffffffffu, tc_wait(&emptyA[sa], pa ^ 1u, abort_flag))) return false;
             tc_fence_after();  // the MMAs that read this A stage have completed
+            // two halves of 32 columns; the second is computed while the first is being stored
+            uint32_t v[2][32];
 #pragma unroll
             for (int p = 0; p < 2; p++) {
                 // 32 bytes of nibbles: low nibbles = sub-block 4*grp+2p, high = 4*grp+2p+1
@@ -458,20 +462,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
                 const uint32_t wq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
                 // columns 0-15: the low sub-block, 16-31: the high one; word 2c+h fills
                 // columns 4c+2h (its elements 0, 2) and 4c+2h+1 (elements 1, 3)
-                uint32_t v[32];
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
 #pragma unroll
                     for (int h = 0; h < 2; h++) {
                         const uint32_t w = wq[2 * c + h];
-                        v[4 * c + 2 * h] = h2u(__hfma2(nib2h(w), slo, mlo));
-                        v[4 * c + 2 * h + 1] = h2u(__hfma2(nib2h(w >> 8), slo, mlo));
-                        v[16 + 4 * c + 2 * h] = h2u(__hfma2(nib2h(w >> 4), shi, mhi));
-                        v[16 + 4 * c + 2 * h + 1] = h2u(__hfma2(nib2h(w >> 12), shi, mhi));
+                        v[p][4 * c + 2 * h] = h2u(__hfma2(nib2h(w), slo, mlo));
+                        v[p][4 * c + 2 * h + 1] = h2u(__hfma2(nib2h(w >> 8), slo, mlo));
+                        v[p][16 + 4 * c + 2 * h] = h2u(__hfma2(nib2h(w >> 4), shi, mhi));
+                        v[p][16 + 4 * c + 2 * h + 1] = h2u(__hfma2(nib2h(w >> 12), shi, mhi));
                     }
                 }
-                tmem_st32(tmem + lane_base + kTcAccCols + kTcAStageCols * uint32_t(sa) + 32u * uint32_t(p), v);
+                tmem_st32_async(tmem + lane_base + kTcAccCols + kTcAStageCols * uint32_t(sa) + 32u * uint32_t(p),
+                                v[p]);
             }
+            tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(cluster_addr(&fullA[sa], 0));
