@@ -185,4 +185,15 @@ __global__ void __launch_bounds__(256) ar_add_kernel(const ArIn ar, const float 
     *reinterpret_cast<float4 *>(o + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
 
+// A zero contribution to the next all-reduce (this rank's slot of every
+// rank's buffer): the producer side of row_block_out with all values 0.
+__global__ void __launch_bounds__(256) ar_zero_kernel(const ArOut ar, int64_t total) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const unsigned e = *ar.seq + 1u;
+    const int64_t slot = (int64_t(e & 1u) * ar.world + ar.rank) * ar.n_max;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x)
+        for (int d = 0; d < ar.world; d++) st_relaxed_sys_u64(ar.peer[d] + slot + i, uint64_t(e) << 32);
+}
+
 }  // namespace cpq

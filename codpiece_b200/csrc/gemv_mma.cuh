@@ -375,18 +375,38 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __gr
                     for (int ng = 0; ng < NG; ng++)
 #pragma unroll
                         for (int i = 0; i < 4; i++) sum[ng][i] = 0.0f;
-                    for (int p = 0; p < npieces; p++) {
-                        const int64_t gp = first + p;
-                        const int sl = (c_mb == (gp * T / G) / nbk) ? 0 : 1;
-                        const float *q = a.partials + (size_t(gp) * 2 + sl) * (kMmaRows * kMmaMaxTokens);
+                    // piece p > 0 starts inside this row block (slot 0); piece 0 uses slot 1 when
+                    // its share began earlier. Loads of a batch of pieces go out together, then
+                    // are added in piece order.
+                    const int first_slot = (first * T / G < c_mb * nbk) ? 1 : 0;
+                    constexpr int kBatch = 4;
+                    for (int p0 = 0; p0 < npieces; p0 += kBatch) {
+                        float pv[kBatch][NG][4];
 #pragma unroll
-                        for (int ng = 0; ng < NG; ng++)
+                        for (int j = 0; j < kBatch; j++) {
+                            if (p0 + j < npieces) {
+                                const int sl = (p0 + j == 0) ? first_slot : 0;
+                                const float *q =
+                                    a.partials + (size_t(first + p0 + j) * 2 + sl) * (kMmaRows * kMmaMaxTokens);
 #pragma unroll
-                            for (int i = 0; i < 4; i++) {
-                                const int t = ng * 8 + 2 * tig + (i & 1);
-                                const int r = gid + 8 * (i >> 1);
-                                sum[ng][i] += __ldcg(q + r * kMmaMaxTokens + t);
+                                for (int ng = 0; ng < NG; ng++)
+#pragma unroll
+                                    for (int i = 0; i < 4; i++) {
+                                        const int t = ng * 8 + 2 * tig + (i & 1);
+                                        const int r = gid + 8 * (i >> 1);
+                                        pv[j][ng][i] = __ldcg(q + r * kMmaMaxTokens + t);
+                                    }
                             }
+                        }
+#pragma unroll
+                        for (int j = 0; j < kBatch; j++) {
+                            if (p0 + j < npieces) {
+#pragma unroll
+                                for (int ng = 0; ng < NG; ng++)
+#pragma unroll
+                                    for (int i = 0; i < 4; i++) sum[ng][i] += pv[j][ng][i];
+                            }
+                        }
                     }
 #pragma unroll
                     for (int ng = 0; ng < NG; ng++)

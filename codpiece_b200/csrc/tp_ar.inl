@@ -154,3 +154,16 @@ extern "C" cpq_status cpq_tp_ar_add(cpq_tp_ar *ar, const float *x, float *out, i
     const cudaError_t e = launch(ar_add_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), in, x, out, k);
     return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "cpq_tp_ar_add: launch");
 }
+
+extern "C" cpq_status cpq_tp_ar_zero(cpq_tp_ar *ar, int64_t n, int64_t m, void *stream) {
+    using namespace cpq;
+    if (!ar) return fail(CPQ_ERR_INVALID_ARG, "cpq_tp_ar_zero: null channel");
+    if (n <= 0 || m <= 0) return fail(CPQ_ERR_INVALID_ARG, "cpq_tp_ar_zero: n=%lld m=%lld", (long long)n, (long long)m);
+    const char *why = "";
+    if (!ar_ready(ar, m * n, &why)) return fail(CPQ_ERR_INVALID_ARG, "cpq_tp_ar_zero: %s", why);
+    const ArOut o = ar_out_of(ar, n);
+    const int64_t total = m * n;
+    const cudaError_t e = launch(ar_zero_kernel, dim3(unsigned(std::min<int64_t>((total + 255) / 256, 1024))),
+                                 dim3(256), 0, static_cast<cudaStream_t>(stream), o, total);
+    return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "cpq_tp_ar_zero: launch");
+}

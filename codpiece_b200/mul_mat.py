@@ -336,6 +336,10 @@ class ArChannel:
                                   _stream(stream)), "cpq_tp_ar_add")
         return out
 
+    def zero(self, n: int, m: int, stream=None) -> None:
+        """Contribute zeros (m tokens x n) to the next all-reduce (a rank without rows of it)."""
+        check(lib().cpq_tp_ar_zero(self.handle, n, m, _stream(stream)), "cpq_tp_ar_zero")
+
     def close(self) -> None:
         if self.handle:
             lib().cpq_tp_ar_destroy(self.handle)

@@ -133,8 +133,7 @@ class Stack:
         # Row-parallel partial sums: through the fused NVLink allreduce when the
         # caller supplies a handle exchange (decode M <= 3 with the head), else NCCL.
         self.ar: mm.ArChannel | None = None
-        if ar_exchange is not None and world > 1 and m <= 3 and head and all(
-                lw.o is not None and lw.down is not None for lw in self.layers):
+        if ar_exchange is not None and world > 1 and m <= 3 and head:
             self.ar = mm.ArChannel(world, rank, m * e, self.dev.index)
             self.ar.connect(list(ar_exchange(self.ar.ipc_handle)))
         if use_plan:
@@ -236,13 +235,17 @@ class Stack:
                 elif ws:
                     mm.mul_mat_fused(ws, h, outs, mode=mm.PRO_RMS, r=self.part, h_out=h_alt, eps=self.eps)
                     h, h_alt = h_alt, h
+                elif ch is not None:
+                    ch.add(h, h)  # no attention rows on this rank: fold the all-reduced residual in place
                 else:
                     mm.add_(h, self.part)  # no attention rows on this rank: fold the residual in place
             elif ws:
                 mm.mul_mat_fused(ws, h, outs, mode=mm.PRO_RMS, eps=self.eps)
             # o projection (row-parallel)
-            if ch is not None:
+            if ch is not None and lw.o is not None:
                 mm.mul_mat_fused([lw.o], self._sl(self.qb, lw.o.k), [self.part], y_ar=ch)
+            elif ch is not None:
+                ch.zero(self.hp.n_embd, self.m)  # no attention rows: a zero share of the all-reduce
             elif lw.o is not None:
                 mm.mul_mat(lw.o, self._sl(self.qb, lw.o.k), out=self.part)
             else:
@@ -259,7 +262,12 @@ class Stack:
                                  eps=self.eps)
             h, h_alt = h_alt, h
             # down (row-parallel) with silu(gate) * up fused into its quantizer
-            mm.mul_mat_fused([lw.down], g, [self.part], mode=mm.PRO_SWIGLU, r=u, y_ar=ch)
+            if lw.down is not None:
+                mm.mul_mat_fused([lw.down], g, [self.part], mode=mm.PRO_SWIGLU, r=u, y_ar=ch)
+            elif ch is not None:
+                ch.zero(self.hp.n_embd, self.m)
+            else:
+                self.part.zero_()
             if self.world > 1 and ch is None:
                 self.comm.allreduce_(self.part)
             part_live = True

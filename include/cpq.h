@@ -291,6 +291,12 @@ void cpq_tp_ar_destroy(cpq_tp_ar *ar);
  * consumers outside the Q4_K decode GEMV (e.g. the Q6_K LM head's residual). */
 cpq_status cpq_tp_ar_add(cpq_tp_ar *ar, const float *x, float *out, int64_t k, int64_t m, void *stream);
 
+/* A zero contribution of n floats per token (m tokens) to the next all-reduce:
+ * for a rank that owns no part of a row-parallel projection in this layer
+ * (at TP8 the attention split leaves half of the ranks without attention
+ * rows), so every rank still produces into every all-reduce. */
+cpq_status cpq_tp_ar_zero(cpq_tp_ar *ar, int64_t n, int64_t m, void *stream);
+
 /* cpq_mul_mat_fused with a channel at either end (either may be NULL):
  *  y_ar  Y_0 (n_w must be 1) is all-reduced through the channel instead of
  *        being stored in y[0] (y[0] still gives the shape);
