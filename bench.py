@@ -242,6 +242,27 @@ def prefill_roofline(torch, mm, reps: int = 10):
             "achieved_is": "FLOP-weighted over the four configs[3] cases", "best": best, "cases": cases}
 
 
+def verify_step(torch, st, tp, layers: int, m: int = 8, steps: int = 10):
+    """configs[4]'s verify step: the same stack at M = 8 tokens (MMA GEMVs, NCCL-free at TP1)."""
+    stack = st.Stack(tp.HP_BENCH_27B, layers, 0, 1, None, m=m, seed=0)
+    stack.h.copy_(torch.randn(m, 5120, device="cuda"))
+    stack.capture()
+    for _ in range(3):
+        stack.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        stack.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    wb = stack.weight_bytes()
+    stack.release()
+    return {"m": m, "ms_per_step": round(ms, 4), "tok_per_s": round(m * 1e3 / ms, 1),
+            "weight_GBs": round(wb / ms / 1e6, 1), "layers": layers}
+
+
 def profile_case(args) -> int:
     """One small fixed case for ncu (see the module docstring)."""
     import torch
@@ -356,6 +377,7 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-verify", action="store_true")
     ap.add_argument("--nccl", action="store_true", help="TP partial sums through NCCL instead of the fused allreduce")
     ap.add_argument("--profile", default=None, choices=["decode_ffn", "prefill_512", "stack"])
     args = ap.parse_args()
@@ -424,11 +446,13 @@ def main() -> int:
     torch.cuda.synchronize()
 
     # ---- timed region: device-resident inputs ----
+    # The sampler starts first so that its process start-up skew between ranks
+    # lands before the barrier, not inside the max-over-ranks window.
     clocks = ClockSampler(local)
-    barrier()
-    torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(cur)
     for _ in range(args.steps):
@@ -470,11 +494,14 @@ def main() -> int:
     total_bytes = float(b[0])
     launches = stack.launches_per_step() * args.steps
 
-    roof = prefill = None
+    roof = prefill = verify = None
     if rank == 0:
         roof = kernel_roofline(torch, mm, cur)
         if not args.no_prefill:
             prefill = prefill_roofline(torch, mm)
+    barrier()
+    if world == 1 and not args.no_verify:
+        verify = verify_step(torch, st, tp, args.layers)
     barrier()
 
     ar_mode = ("none" if world == 1 else "nccl" if stack.ar is None else
@@ -513,6 +540,7 @@ def main() -> int:
         "roofline": roof,
         "cpu_baseline": cpu,
         "prefill": prefill,
+        "verify": verify,
     }
     print(json.dumps(line), flush=True)
     return 0
