@@ -32,17 +32,21 @@ static cpq_status cuda_fail(cudaError_t e, const char *what) {
 
 constexpr int kMaxDevices = 64;
 
-// Workspace carve-up: [row-block counters][per-warp partials][activations].
-// The counters must be zero before the first call; the MMA kernel leaves
-// them zero after every successful call.
+// Workspace carve-up: [row-block counters][per-warp partials][per-warp piece
+// words][argmax scratch][activations]. The counters and piece words must be
+// zero before the first call; the GEMV kernels leave them zero after every
+// successful call (cpq_device_status with clear also re-zeroes them).
 constexpr size_t kWsCounters = 65536;                       // row blocks per call (>= 1M rows)
 constexpr size_t kWsCountersBytes = kWsCounters * sizeof(int);
 constexpr size_t kWsMaxWarps = 148 * 2 * 16;                // persistent warps, generous
 constexpr size_t kWsPartialBytes = kWsMaxWarps * 2 * 16 * 16 * sizeof(float);
 constexpr int kArgmaxChunks = 128;                            // CTAs per argmax row
 constexpr int kArgmaxMaxRows = 64;
+constexpr size_t kWsPieceBytes = kWsMaxWarps * 2 * kPieceWords * sizeof(uint64_t);  // row GEMV (gemv_row.cuh)
 constexpr size_t kWsAuxBytes = align_up(size_t(kArgmaxMaxRows) * (kArgmaxChunks * 8 + 4), 256);
-constexpr size_t kWsActOffset = kWsCountersBytes + kWsPartialBytes + kWsAuxBytes;
+constexpr size_t kWsPieceOffset = kWsCountersBytes + kWsPartialBytes;
+constexpr size_t kWsAuxOffset = kWsPieceOffset + kWsPieceBytes;
+constexpr size_t kWsActOffset = kWsAuxOffset + kWsAuxBytes;
 
 struct DevState {
     void *ws = nullptr;
@@ -401,7 +405,17 @@ static size_t frag_bytes(int64_t k, int mp) {
 
 constexpr int kSmemMax = 227 * 1024;
 
-static int row_smem_bytes(int64_t k, int mt) { return kRowBarBytes + row_act_bytes(k, mt) + kRowRingBytes; }
+static int row_smem_bytes(int64_t k, int mt) {
+    return kRowBarBytes + row_act_bytes(k, mt) + kRowRingBytes + row_red_bytes(mt);
+}
+
+// CTAs of the row GEMV: one per SM at most (the kernel's tail-cut hand-off
+// needs every CTA resident), and at most T / nbk so that no CTA's range lies
+// inside one row block.
+static int64_t row_grid(const RowArgs &a, int64_t cap) {
+    const int64_t row_blocks = a.mb_start[a.n_w];
+    return std::max<int64_t>(1, std::min<int64_t>(cap, row_blocks));
+}
 
 template <int MT>
 static cudaError_t launch_q4k_row_t(RowArgs &a, int smem, cudaStream_t st) {
@@ -414,10 +428,7 @@ static cudaError_t launch_q4k_row_t(RowArgs &a, int smem, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         set[dev].store(1, std::memory_order_relaxed);
     }
-    const int64_t T = a.mb_start[a.n_w] * a.nbk;
-    const int64_t cap = std::min<int64_t>(int64_t(sm_count(dev)) * kRowWarps, int64_t(kWsMaxWarps));
-    a.n_warps = std::max<int64_t>(1, std::min<int64_t>(cap, T));
-    const int64_t grid = (a.n_warps + kRowWarps - 1) / kRowWarps;
+    const int64_t grid = row_grid(a, std::min<int64_t>(sm_count(dev), int64_t(kWsMaxWarps / kRowWarps)));
     return launch(kern, dim3(unsigned(grid)), dim3(kRowWarps * 32), size_t(smem), st, a);
 }
 
@@ -465,8 +476,7 @@ static cpq_status run_q4k_row(const GemvArgs &g, const float *x, int64_t x_strid
     a.nbk = nbk;
     a.m = m;
     a.act = act;
-    a.partials = reinterpret_cast<float *>(ws + kWsCountersBytes);
-    a.counters = reinterpret_cast<int *>(ws);
+    a.pieces = reinterpret_cast<uint64_t *>(ws + kWsPieceOffset);
     if (ar_out) a.ar = *ar_out;
     const int smem = row_smem_bytes(k, m);
     switch (m) {
@@ -894,7 +904,7 @@ cpq_status cpq_argmax(const float *x, int64_t n, int64_t m, int32_t *out, void *
     cpq_status rc = workspace_of_current(&ws, &bytes);
     if (rc) return rc;
     // aux area after the row-block counters and partials: [rows][chunks] values, indices, then row counters
-    uint8_t *aux = static_cast<uint8_t *>(ws) + kWsCountersBytes + kWsPartialBytes;
+    uint8_t *aux = static_cast<uint8_t *>(ws) + kWsAuxOffset;
     float *pval = reinterpret_cast<float *>(aux);
     int32_t *pidx = reinterpret_cast<int32_t *>(aux + size_t(kArgmaxMaxRows) * kArgmaxChunks * 4);
     int *cnt = reinterpret_cast<int *>(aux + size_t(kArgmaxMaxRows) * kArgmaxChunks * 8);
@@ -919,8 +929,13 @@ cpq_status cpq_synth_weights(int32_t type, void *dst, int64_t n_rows, int64_t n_
     return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "synth launch");
 }
 
+namespace cpq {
+static cudaError_t noalloc_clear_scratch();  // noalloc.inl
+}
+
 cpq_status cpq_device_status(int device, uint32_t *err_word, int clear) {
     if (!err_word) return fail(CPQ_ERR_INVALID_ARG, "err_word is null");
+    if (device < 0 || device >= kMaxDevices) return fail(CPQ_ERR_INVALID_ARG, "device %d out of range", device);
     int prev = 0;
     cudaGetDevice(&prev);
     cudaError_t e = cudaSetDevice(device);
@@ -928,8 +943,14 @@ cpq_status cpq_device_status(int device, uint32_t *err_word, int clear) {
     e = cudaDeviceSynchronize();
     if (e == cudaSuccess) e = cudaMemcpyFromSymbol(err_word, g_dev_error, sizeof(uint32_t));
     if (e == cudaSuccess && clear) {
+        // A call that gave up may have left stream-K counters and piece words
+        // set: both scratch areas go back to zero with the error word.
         const uint32_t z = 0;
         e = cudaMemcpyToSymbol(g_dev_error, &z, sizeof z);
+        if (e == cudaSuccess) e = noalloc_clear_scratch();
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (e == cudaSuccess && g_dev[device].ws) e = cudaMemset(g_dev[device].ws, 0, kWsActOffset);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
     }
     cudaSetDevice(prev);
     if (e != cudaSuccess) return cuda_fail(e, "device status");

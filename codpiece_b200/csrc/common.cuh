@@ -213,6 +213,48 @@ struct ArRows {
     unsigned seq;
 };
 
+// ---- flagged words between the CTAs of one grid ----------------------------
+//
+// A 64-bit word (flag << 32 | 32-bit payload) is stored and loaded whole, so a
+// reader that sees the flag also sees the payload: nothing has to be fenced
+// before the word is published.
+
+__device__ __forceinline__ void st_relaxed_gpu_u64(uint64_t *p, uint64_t v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_gpu_u64(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Counter increment without ordering: its result is only used to elect the
+// last arriver, whose reads wait on flagged words instead of on a fence.
+__device__ __forceinline__ int atom_add_relaxed_gpu(int *p, int v) {
+    int old;
+    asm volatile("atom.relaxed.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// The word at p once its high half equals flag (bounded wait; on give-up the
+// device error word is set and flag << 32 is returned, a payload of 0). Once a
+// wait on this device has given up, later words are not waited for.
+__device__ __forceinline__ uint64_t flagged_word_gpu(const uint64_t *p, uint32_t flag) {
+    uint64_t w = ld_relaxed_gpu_u64(p);
+    if (uint32_t(w >> 32) == flag) return w;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1;; ++it) {
+        w = ld_relaxed_gpu_u64(p);
+        if (uint32_t(w >> 32) == flag) return w;
+        if ((it & 63u) == 0 && ((*reinterpret_cast<volatile uint32_t *>(&g_dev_error) & kDevErrWaitTimeout) ||
+                                global_timer_ns() - t0 > kWaitLimitNs)) {
+            atomicOr(&g_dev_error, kDevErrWaitTimeout);
+            return uint64_t(flag) << 32;
+        }
+    }
+}
+
 __device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *p, uint64_t v) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }

@@ -70,7 +70,7 @@ struct DecArgs {
     int n_ph;
     int act_bytes;       // shared-memory activation region (largest phase image)
     uint8_t *act_g;      // global activation image (act_bytes)
-    float *partials;     // [warp][2][256]
+    uint64_t *pieces;    // [warp][2][kPieceWords] stream-K piece words, zero between phases
     int *counters;       // [row block], zero between phases
     unsigned *bar;       // grid barrier counter, zero at launch
 };
@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(kDecWarps * 32, 1) decode_step_kernel(const __
         int64_t c_it, c_end;
         share(p, c_it, c_end);
         const int64_t T = (n_w == 1 ? mb1 : n_w == 2 ? mb2 : mb3) * nbk;
-        const RowSeg sg{G, T, g, c_it / nbk, a.partials, a.counters};
+        const RowSeg sg{G, T, g, c_it / nbk, a.pieces, a.counters};
         int64_t c_mb = c_it / nbk;
         int c_kb = int(c_it - c_mb * nbk);
         int64_t seg_start = c_it;

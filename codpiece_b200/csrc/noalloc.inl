@@ -7,8 +7,8 @@
 // touching cudaMalloc, and latency-critical threads that must not hit the
 // implicit device synchronization a cudaMalloc/cudaFree can cause. For them
 // this entry point runs the decode GEMV (gemv_row.cuh, unchanged) with every
-// byte of its scratch — the quantized activation image, the stream-K partial
-// sums and the row-block counters — in one file-scope device array that is
+// byte of its scratch — the quantized activation image and the tail-cut
+// words the CTAs hand each other — in one file-scope device array that is
 // reserved when the library is loaded and held by every GPU that loads it
 // until the process exits.
 //
@@ -18,10 +18,9 @@
 // that pointer. The first call on a device performs this set-up, so make the
 // first call before any stream capture.
 //
-// Every call shares the one array and it keeps the previous call's contents:
-// the counters are cleared (cudaMemsetAsync on the calling stream, no
-// allocation) at the start of every call, and calls whose executions overlap
-// on the GPU (e.g. on two streams at once) race on the array.
+// Every call shares the one array: the tail-cut words are zero between calls
+// (each call clears what it reads), and calls whose executions overlap on the
+// GPU (e.g. on two streams at once) race on the array.
 #include <mutex>
 
 namespace cpq {
@@ -30,11 +29,10 @@ namespace cpq {
 constexpr int64_t kNoAllocMaxRows = 262144;  // N (output rows)
 constexpr int64_t kNoAllocMaxK = 32768;      // K
 constexpr int kNoAllocMaxTokens = kRowMaxTokens;
-constexpr int64_t kNoAllocMaxWarps = 148 * kRowWarps;  // persistent warps given partial slots
-constexpr size_t kNoAllocCounterBytes = align_up(size_t(kNoAllocMaxRows / kRowRows) * sizeof(int), 256);
-constexpr size_t kNoAllocPartialBytes = size_t(kNoAllocMaxWarps) * 2 * 256 * sizeof(float);
+constexpr int64_t kNoAllocMaxCtas = 148;  // CTAs given tail-cut slots (larger parts run on 148 SMs)
+constexpr size_t kNoAllocPieceBytes = size_t(kNoAllocMaxCtas) * kRowWarps * kPieceWords * sizeof(uint64_t);
 constexpr size_t kNoAllocActBytes = align_up(size_t(row_act_bytes(kNoAllocMaxK, kNoAllocMaxTokens)), 256);
-constexpr size_t kNoAllocBytes = kNoAllocCounterBytes + kNoAllocPartialBytes + kNoAllocActBytes;  // ~2.5 MB
+constexpr size_t kNoAllocBytes = kNoAllocPieceBytes + kNoAllocActBytes;  // ~1.4 MB
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
@@ -55,6 +53,15 @@ static cpq_status noalloc_scratch(uint8_t **out) {
     return CPQ_SUCCESS;
 }
 
+// Zeroes the tail-cut words of the current device's static scratch
+// (after a device-side timeout left a call unfinished).
+static cudaError_t noalloc_clear_scratch() {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, kNoAllocPieceBytes);
+    return e;
+}
+
 template <int MT>
 static cudaError_t noalloc_launch_row(RowArgs &a, int smem, cudaStream_t st) {
     auto kern = gemv_q4k_row_kernel<MT>;
@@ -62,10 +69,7 @@ static cudaError_t noalloc_launch_row(RowArgs &a, int smem, cudaStream_t st) {
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
     if (e != cudaSuccess) return e;
-    const int64_t T = a.mb_start[a.n_w] * a.nbk;
-    const int64_t cap = std::min<int64_t>(int64_t(sm_count(dev)) * kRowWarps, kNoAllocMaxWarps);
-    a.n_warps = std::max<int64_t>(1, std::min<int64_t>(cap, T));
-    const int64_t grid = (a.n_warps + kRowWarps - 1) / kRowWarps;
+    const int64_t grid = row_grid(a, std::min<int64_t>(sm_count(dev), kNoAllocMaxCtas));
     return launch(kern, dim3(unsigned(grid)), dim3(kRowWarps * 32), size_t(smem), st, a);
 }
 
@@ -98,9 +102,8 @@ extern "C" cpq_status cpq_mul_mat_noalloc(const cpq_tensor *w, const cpq_tensor 
 
     uint8_t *scratch = nullptr;
     if ((rc = noalloc_scratch(&scratch))) return rc;
-    uint8_t *counters = scratch;
-    uint8_t *partials = scratch + kNoAllocCounterBytes;
-    uint8_t *act = partials + kNoAllocPartialBytes;
+    uint8_t *pieces = scratch;
+    uint8_t *act = pieces + kNoAllocPieceBytes;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
 
     static thread_local RowArgs a;
@@ -115,11 +118,8 @@ extern "C" cpq_status cpq_mul_mat_noalloc(const cpq_tensor *w, const cpq_tensor 
     a.nbk = int(s.k / kQK_K);
     a.m = int(m);
     a.act = act;
-    a.partials = reinterpret_cast<float *>(partials);
-    a.counters = reinterpret_cast<int *>(counters);
+    a.pieces = reinterpret_cast<uint64_t *>(pieces);
 
-    cudaError_t e = cudaMemsetAsync(counters, 0, kNoAllocCounterBytes, st);
-    if (e != cudaSuccess) return cuda_fail(e, "cpq_mul_mat_noalloc: clearing the counters");
     ActPrepArgs pa = {};
     pa.mode = kActPlain;
     pa.x = static_cast<const float *>(x->data);
@@ -131,7 +131,7 @@ extern "C" cpq_status cpq_mul_mat_noalloc(const cpq_tensor *w, const cpq_tensor 
     pa.m = int(m);
     pa.eps = 0.0f;
     pa.out = act;
-    e = launch(act_prep_kernel, dim3(unsigned((a.nbk + 7) / 8), unsigned(m)), dim3(256), 0, st, pa);
+    cudaError_t e = launch(act_prep_kernel, dim3(unsigned((a.nbk + 7) / 8), unsigned(m)), dim3(256), 0, st, pa);
     if (e != cudaSuccess) return cuda_fail(e, "cpq_mul_mat_noalloc: act_prep launch");
     switch (m) {
     case 1: e = noalloc_launch_row<1>(a, smem, st); break;

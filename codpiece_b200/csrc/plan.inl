@@ -2,7 +2,7 @@
 //
 // A plan is the device-side description of a decode chain: one DecPhase per
 // phase, one DecWeight (TMA tensor map + output pointer) per weight, the
-// stream-K scratch (per-warp partial slots, per-row-block counters) and the
+// stream-K scratch (per-warp piece words, per-row-block counters) and the
 // grid-barrier counter. Creating it validates every phase with the same
 // checks as cpq_mul_mat_fused; running it clears the counters and the
 // barrier and launches one cooperative grid of one CTA per SM.
@@ -15,7 +15,7 @@ struct cpq_decode_plan {
     int act_bytes = 0;
     cpq::DecPhase *d_ph = nullptr;
     cpq::DecWeight *d_w = nullptr;
-    float *partials = nullptr;
+    uint64_t *pieces = nullptr;
     int *counters = nullptr;
     size_t counter_bytes = 0;
     unsigned *bar = nullptr;
@@ -31,7 +31,7 @@ static void plan_free(cpq_decode_plan *p) {
     if (p->device >= 0) cudaSetDevice(p->device);
     cudaFree(p->d_ph);
     cudaFree(p->d_w);
-    cudaFree(p->partials);
+    cudaFree(p->pieces);
     cudaFree(p->counters);
     cudaFree(p->bar);
     cudaFree(p->act_g);
@@ -138,16 +138,17 @@ extern "C" cpq_status cpq_decode_plan_create(const cpq_decode_phase *phases, int
     if (e != cudaSuccess || per_sm < 1) return done(fail(CPQ_ERR_CUDA, "decode plan: kernel does not fit on an SM"));
     p->grid = sm_count(device);
     p->counter_bytes = align_up(size_t(max_mb) * sizeof(int), 256);
-    const size_t partial_bytes = size_t(p->grid) * kDecWarps * 2 * 256 * sizeof(float);
+    const size_t piece_bytes = size_t(p->grid) * kDecWarps * 2 * kPieceWords * sizeof(uint64_t);
     if ((e = cudaMalloc(&p->d_ph, ph.size() * sizeof(DecPhase))) != cudaSuccess ||
         (e = cudaMalloc(&p->d_w, wt.size() * sizeof(DecWeight))) != cudaSuccess ||
-        (e = cudaMalloc(&p->partials, partial_bytes)) != cudaSuccess ||
+        (e = cudaMalloc(&p->pieces, piece_bytes)) != cudaSuccess ||
         (e = cudaMalloc(&p->counters, p->counter_bytes)) != cudaSuccess ||
         (e = cudaMalloc(&p->bar, 256)) != cudaSuccess ||
         (e = cudaMalloc(&p->act_g, size_t(act_bytes))) != cudaSuccess)
         return done(cuda_fail(e, "decode plan: cudaMalloc"));
     if ((e = cudaMemcpy(p->d_ph, ph.data(), ph.size() * sizeof(DecPhase), cudaMemcpyHostToDevice)) != cudaSuccess ||
-        (e = cudaMemcpy(p->d_w, wt.data(), wt.size() * sizeof(DecWeight), cudaMemcpyHostToDevice)) != cudaSuccess)
+        (e = cudaMemcpy(p->d_w, wt.data(), wt.size() * sizeof(DecWeight), cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (e = cudaMemset(p->pieces, 0, piece_bytes)) != cudaSuccess)
         return done(cuda_fail(e, "decode plan: table upload"));
     *out = p;
     return done(CPQ_SUCCESS);
@@ -168,7 +169,7 @@ extern "C" cpq_status cpq_decode_plan_run(cpq_decode_plan *p, void *stream) {
     a.w = p->d_w;
     a.n_ph = p->n_ph;
     a.act_bytes = p->act_bytes;
-    a.partials = p->partials;
+    a.pieces = p->pieces;
     a.counters = p->counters;
     a.bar = p->bar;
     a.act_g = p->act_g;

@@ -322,7 +322,11 @@ cpq_status cpq_synth_weights(int32_t type, void *dst, int64_t n_rows, int64_t n_
 /* ---- diagnostics ------------------------------------------------------------ */
 
 /* Reads (and with clear != 0 resets) the device-side error word that kernels
- * set when a bounded wait gives up. Synchronizes the device. */
+ * set when a bounded wait gives up. Synchronizes the device. Clearing also
+ * zeroes the stream-K scratch (counters, piece words) of the device's
+ * workspace and of cpq_mul_mat_noalloc, which a call that gave up may have
+ * left set; a caller-provided workspace (cpq_mul_mat_ws) must be re-zeroed
+ * by its owner. */
 cpq_status cpq_device_status(int device, uint32_t *err_word, int clear);
 const char *cpq_last_error(void);
 const char *cpq_status_string(cpq_status s);

@@ -1,10 +1,14 @@
 """GPU: decode plans (cpq_decode_plan_*), the persistent decode kernel.
 
-A plan runs the same arithmetic with the same stream-K split as the
-separate act_prep + row-GEMV launches (one warp per 32-row block and
-superblock range, 8 warps per SM), so its outputs are compared bit for bit
-with those launches, and the stack built on a plan against the CPU
-restatement like the per-call stack.
+A plan runs the same arithmetic as the separate act_prep + row-GEMV
+launches, but splits the work differently (a stream-K share per warp across
+the whole grid, where the per-call GEMV gives each CTA a range): the
+superblock dot products are the same and only the order in which they are
+summed differs. So a plan's outputs are compared with those launches to
+within fp32 summation-order error for the first phase (identical inputs) and
+to the parity tolerance down the chain (a last-bit difference can move one
+Q8_K rounding), plan against plan bit for bit, and the stack built on a plan
+against the CPU restatement like the per-call stack.
 """
 import ctypes as C
 
@@ -21,7 +25,7 @@ def _mm():
     return mm
 
 
-def test_plan_phases_equal_separate_calls(cuda):
+def test_plan_phases_match_separate_calls(cuda):
     """RMS with residual and h_out, a plain phase, a SwiGLU phase; three weights in one phase."""
     torch = cuda
     mm = _mm()
@@ -58,17 +62,20 @@ def test_plan_phases_equal_separate_calls(cuda):
     (d2,) = mm.mul_mat_fused([wd], g2, mode=mm.PRO_SWIGLU, r=u2)
     torch.cuda.synchronize()
     assert torch.equal(hh, hh2.view(-1))
-    for a, b in ((yq, q2), (yk, k2), (yv, v2), (yo, o2), (yg, g2), (yu, u2), (yd, d2)):
-        assert torch.equal(a, b.view(-1))
-    # and again (counters and the grid barrier are reset by every run)
+    for a, b in ((yq, q2), (yk, k2), (yv, v2)):  # same image: summation order only
+        assert rel_err(a.cpu().numpy(), b.view(-1).cpu().numpy()) <= 1e-5
+    for a, b in ((yo, o2), (yg, g2), (yu, u2), (yd, d2)):
+        assert rel_err(a.cpu().numpy(), b.view(-1).cpu().numpy()) <= TOL
+    # and again (counters and the grid barrier are reset by every run): bit for bit
+    yd_first = yd.clone()
     yd.zero_()
     plan.run()
     torch.cuda.synchronize()
-    assert torch.equal(yd, d2.view(-1))
+    assert torch.equal(yd, yd_first)
     plan.close()
 
 
-def test_plan_stack_equals_per_call_stack(cuda):
+def test_plan_stack_matches_per_call_stack(cuda):
     from codpiece_b200 import stack as st
     from codpiece_b200 import tp
 
@@ -82,9 +89,12 @@ def test_plan_stack_equals_per_call_stack(cuda):
         torch.cuda.synchronize()
         outs.append((s.h_final.clone(), s.logits.clone(), s.tok.clone()))
         s.release()
-    assert torch.equal(outs[0][0], outs[1][0])
-    assert torch.equal(outs[0][1], outs[1][1])
-    assert torch.equal(outs[0][2], outs[1][2])
+    assert rel_err(outs[0][0].cpu().numpy(), outs[1][0].cpu().numpy()) <= TOL
+    assert rel_err(outs[0][1].cpu().numpy(), outs[1][1].cpu().numpy()) <= TOL
+    # the same token, unless the two top logits are within the tolerance of each other
+    t0, t1 = int(outs[0][2].view(-1)[0]), int(outs[1][2].view(-1)[0])
+    lg = outs[0][1].view(-1)
+    assert t0 == t1 or abs(float(lg[t0] - lg[t1])) <= TOL * float(lg.abs().max())
 
 
 def test_plan_stack_matches_cpu_restatement_and_replays(cuda, oracle):
