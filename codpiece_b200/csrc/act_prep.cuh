@@ -67,13 +67,7 @@ __device__ __forceinline__ void act_load_v(int mode, const float *xr, const floa
     if (mode == kActRms) {
         if (ar) {
             float rv[8];
-            ar_words8(ar->p0 + e0, ar->seq, rv);
-            for (int s = 1; s < ar->n; s++) {
-                float q[8];
-                ar_words8(ar->p0 + s * ar->stride + e0, ar->seq, q);
-#pragma unroll
-                for (int e = 0; e < 8; e++) rv[e] = __fadd_rn(rv[e], q[e]);
-            }
+            ar_sum8(ar->p0 + e0, ar->stride, ar->n, ar->seq, rv);
 #pragma unroll
             for (int e = 0; e < 8; e++) v[e] = __fadd_rn(v[e], rv[e]);
         } else if (rr) {
@@ -194,9 +188,10 @@ __global__ void __launch_bounds__(256, 1) act_prep_kernel(const ActPrepArgs a) {
     const float *rr = a.r ? a.r + t * a.x_stride : nullptr;
     ArRows rows;
     const ArRows *arp = nullptr;
+    unsigned ticket = 0;
     if (a.ar.on) {
         // r = the sum over ranks of the all-reduced output (LL words, waited for one by one)
-        if (threadIdx.x == 0) ar_seq = ar_consumer_seq(a.ar);
+        if (threadIdx.x == 0) ar_seq = ar_consumer_begin(a.ar, ticket);
         __syncthreads();
         const int par = int(ar_seq & 1u);
         rows.n = a.ar.world;
@@ -206,17 +201,26 @@ __global__ void __launch_bounds__(256, 1) act_prep_kernel(const ActPrepArgs a) {
         arp = &rows;
     }
     float scale = 1.0f;
-    if (a.mode == kActRms) {
-        float vk[kActBatch][8];
-        act_rms_row<false>(xr, rr, a.k, a.eps, part, scale, vk, arp);
-    }
+    float vk[kActBatch][8];
+    bool have = false;
+    if (a.mode == kActRms) have = act_rms_row<false>(xr, rr, a.k, a.eps, part, scale, vk, arp);
     const int b = blockIdx.x * 8 + warp;
     if (b >= nbk) return;
     float v[8];
-    act_load_v<false>(a.mode, xr, rr, b, v, arp);
+    if (have) {  // block b is this warp's block number blockIdx.x of the row pass: reuse its values
+#pragma unroll
+        for (int jj = 0; jj < kActBatch; jj++)
+            if (jj == int(blockIdx.x)) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) v[e] = vk[jj][e];
+            }
+    } else {
+        act_load_v<false>(a.mode, xr, rr, b, v, arp);
+    }
     if (a.mode == kActRms && (rr || arp) && a.h_out)
         store8(a.h_out + t * a.x_stride + int64_t(b) * kQK_K + (threadIdx.x & 31) * 8, v);
     act_quantize_store(a.mode, v, scale, a.g, b, t, a.k, a.m, a.out);
+    if (a.ar.on && threadIdx.x == 0) ar_consumer_end(a.ar, ticket, ar_seq);  // thread 0's block is always < nbk
 }
 
 }  // namespace cpq

@@ -290,28 +290,49 @@ __device__ __forceinline__ void ld_relaxed_sys_v2u64(const uint64_t *p, uint64_t
     asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
-// Eight consecutive LL words (16-byte aligned) of one rank: the loads are
-// issued together, then any word without the expected sequence number is
-// waited for on its own.
-__device__ __forceinline__ void ar_words8(const uint64_t *p, unsigned seq, float (&v)[8]) {
-    uint64_t w[8];
+// The sum over ranks 0..n-1, in rank order, of eight consecutive LL words
+// (rank s at p + s * stride, 16-byte aligned). Every rank's loads are issued
+// before any is looked at, so the ranks cost one memory round trip, not n;
+// a word without the expected sequence number is then waited for on its own.
+__device__ __forceinline__ void ar_sum8(const uint64_t *p, int64_t stride, int n, unsigned seq, float (&v)[8]) {
+    uint64_t w[kArMaxRanks][8];
 #pragma unroll
-    for (int i = 0; i < 4; i++) ld_relaxed_sys_v2u64(p + 2 * i, w[2 * i], w[2 * i + 1]);
+    for (int s = 0; s < kArMaxRanks; s++)
+        if (s < n) {
 #pragma unroll
-    for (int i = 0; i < 8; i++)
-        v[i] = unsigned(w[i] >> 32) == seq ? __uint_as_float(unsigned(w[i])) : ar_word(p + i, seq);
+            for (int i = 0; i < 4; i++) ld_relaxed_sys_v2u64(p + s * stride + 2 * i, w[s][2 * i], w[s][2 * i + 1]);
+        }
+#pragma unroll
+    for (int s = 0; s < kArMaxRanks; s++)
+        if (s < n) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float q =
+                    unsigned(w[s][i] >> 32) == seq ? __uint_as_float(unsigned(w[s][i])) : ar_word(p + s * stride + i, seq);
+                v[i] = s == 0 ? q : __fadd_rn(v[i], q);
+            }
+        }
 }
 
-// Thread 0 of every consumer CTA: this call's sequence number; the last CTA
-// to read it advances the rank's count for the next all-reduce.
-__device__ __forceinline__ unsigned ar_consumer_seq(const ArIn &ar) {
-    const unsigned s = *reinterpret_cast<volatile unsigned *>(ar.seq) + 1u;
-    __threadfence();
-    if (atomicAdd(ar.arrive, 1u) == ar.n_ctas - 1) {
+// Thread 0 of every consumer CTA, first: this call's sequence number. The
+// load is an acquire, so the arrival after it cannot overtake it; the
+// arrival's result (ticket) is only looked at by ar_consumer_end, so its
+// round trip overlaps the CTA's reads of the words.
+__device__ __forceinline__ unsigned ar_consumer_begin(const ArIn &ar, unsigned &ticket) {
+    unsigned s;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(s) : "l"(ar.seq) : "memory");
+    ticket = atomicAdd(ar.arrive, 1u);
+    return s + 1u;
+}
+
+// Thread 0 of every consumer CTA, last: the CTA that arrived last (every other
+// CTA has read the sequence number by then) advances the rank's count for the
+// next all-reduce.
+__device__ __forceinline__ void ar_consumer_end(const ArIn &ar, unsigned ticket, unsigned s) {
+    if (ticket == ar.n_ctas - 1) {
         *ar.arrive = 0u;
         *reinterpret_cast<volatile unsigned *>(ar.seq) = s;
     }
-    return s;
 }
 
 // ---- activation views ------------------------------------------------------

@@ -156,25 +156,20 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float *__restrict__ x
 // out = x + sum over ranks of the channel's last all-reduced value (rank
 // order, the same additions as act_load_v). grid: (ceil(k / 2048), m), 256
 // threads x 8 elements.
-__global__ void __launch_bounds__(256) ar_add_kernel(const ArIn ar, const float *__restrict__ x,
+__global__ void __launch_bounds__(256, 1) ar_add_kernel(const ArIn ar, const float *__restrict__ x,
                                                      float *__restrict__ out, int64_t k) {
     pdl_wait();
     pdl_launch_dependents();
     __shared__ unsigned seq;
-    if (threadIdx.x == 0) seq = ar_consumer_seq(ar);
+    unsigned ticket = 0;
+    if (threadIdx.x == 0) seq = ar_consumer_begin(ar, ticket);
     __syncthreads();
     const int t = blockIdx.y;
     const int64_t e0 = (int64_t(blockIdx.x) * 256 + threadIdx.x) * 8;
     if (e0 >= k) return;
     const uint64_t *base = ar.base + int64_t(seq & 1u) * ar.world * ar.n_max + int64_t(t) * ar.n + e0;
     float v[8];
-    ar_words8(base, seq, v);
-    for (int s = 1; s < ar.world; s++) {
-        float q[8];
-        ar_words8(base + int64_t(s) * ar.n_max, seq, q);
-#pragma unroll
-        for (int e = 0; e < 8; e++) v[e] = __fadd_rn(v[e], q[e]);
-    }
+    ar_sum8(base, ar.n_max, ar.world, seq, v);
     const float4 x0 = *reinterpret_cast<const float4 *>(x + int64_t(t) * k + e0);
     const float4 x1 = *reinterpret_cast<const float4 *>(x + int64_t(t) * k + e0 + 4);
     const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
@@ -183,6 +178,7 @@ __global__ void __launch_bounds__(256) ar_add_kernel(const ArIn ar, const float 
     float *o = out + int64_t(t) * k + e0;
     *reinterpret_cast<float4 *>(o) = make_float4(v[0], v[1], v[2], v[3]);
     *reinterpret_cast<float4 *>(o + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    if (threadIdx.x == 0) ar_consumer_end(ar, ticket, seq);  // thread 0's e0 is always < k
 }
 
 // A zero contribution to the next all-reduce (this rank's slot of every
