@@ -172,6 +172,10 @@ __device__ __forceinline__ bool act_rms_row(const float *xr, const float *rr, in
 }
 
 // grid: (ceil(nbk / 8), m); block 256 = 8 warps, warp w quantizes block 8*blockIdx.x + w of token blockIdx.y
+// AR: the input's residual comes from an all-reduce channel (a.ar); the
+// instance without it carries none of that code, so it stays small enough
+// to share an SM with a GEMV CTA while it waits.
+template <bool AR>
 __global__ void __launch_bounds__(256, 1) act_prep_kernel(const ActPrepArgs a) {
     // Dependents (the row GEMV) may launch before this kernel even starts
     // waiting: they only prefetch weights until their own griddepcontrol.wait,
@@ -189,7 +193,7 @@ __global__ void __launch_bounds__(256, 1) act_prep_kernel(const ActPrepArgs a) {
     ArRows rows;
     const ArRows *arp = nullptr;
     unsigned ticket = 0;
-    if (a.ar.on) {
+    if (AR) {
         // r = the sum over ranks of the all-reduced output (LL words, waited for one by one)
         if (threadIdx.x == 0) ar_seq = ar_consumer_begin(a.ar, ticket);
         __syncthreads();
@@ -220,7 +224,7 @@ __global__ void __launch_bounds__(256, 1) act_prep_kernel(const ActPrepArgs a) {
     if (a.mode == kActRms && (rr || arp) && a.h_out)
         store8(a.h_out + t * a.x_stride + int64_t(b) * kQK_K + (threadIdx.x & 31) * 8, v);
     act_quantize_store(a.mode, v, scale, a.g, b, t, a.k, a.m, a.out);
-    if (a.ar.on && threadIdx.x == 0) ar_consumer_end(a.ar, ticket, ar_seq);  // thread 0's block is always < nbk
+    if (AR && threadIdx.x == 0) ar_consumer_end(a.ar, ticket, ar_seq);  // thread 0's block is always < nbk
 }
 
 }  // namespace cpq

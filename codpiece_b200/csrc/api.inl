@@ -471,7 +471,8 @@ static cpq_status run_q4k_row(const GemvArgs &g, const float *x, int64_t x_strid
         pa.ar = *ar_in;
         pa.ar.n_ctas = unsigned((nbk + 7) / 8) * unsigned(m);  // act_prep_kernel's grid below
     }
-    cudaError_t e = launch(act_prep_kernel, dim3(unsigned((nbk + 7) / 8), unsigned(m)), dim3(256), 0, st, pa);
+    cudaError_t e = ar_in ? launch(act_prep_kernel<true>, dim3(unsigned((nbk + 7) / 8), unsigned(m)), dim3(256), 0, st, pa)
+                          : launch(act_prep_kernel<false>, dim3(unsigned((nbk + 7) / 8), unsigned(m)), dim3(256), 0, st, pa);
     if (e != cudaSuccess) return cuda_fail(e, "act_prep launch");
     a.nbk = nbk;
     a.m = m;

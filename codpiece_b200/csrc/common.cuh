@@ -291,27 +291,32 @@ __device__ __forceinline__ void ld_relaxed_sys_v2u64(const uint64_t *p, uint64_t
 }
 
 // The sum over ranks 0..n-1, in rank order, of eight consecutive LL words
-// (rank s at p + s * stride, 16-byte aligned). Every rank's loads are issued
-// before any is looked at, so the ranks cost one memory round trip, not n;
-// a word without the expected sequence number is then waited for on its own.
+// (rank s at p + s * stride, 16-byte aligned). The loads of kArRound ranks
+// are issued before any is looked at, so n ranks cost ceil(n / kArRound)
+// memory round trips, not n; a word without the expected sequence number is
+// then waited for on its own.
+constexpr int kArRound = 4;
 __device__ __forceinline__ void ar_sum8(const uint64_t *p, int64_t stride, int n, unsigned seq, float (&v)[8]) {
-    uint64_t w[kArMaxRanks][8];
+    for (int s0 = 0; s0 < n; s0 += kArRound) {
+        uint64_t w[kArRound][8];
 #pragma unroll
-    for (int s = 0; s < kArMaxRanks; s++)
-        if (s < n) {
+        for (int s = 0; s < kArRound; s++)
+            if (s0 + s < n) {
 #pragma unroll
-            for (int i = 0; i < 4; i++) ld_relaxed_sys_v2u64(p + s * stride + 2 * i, w[s][2 * i], w[s][2 * i + 1]);
-        }
-#pragma unroll
-    for (int s = 0; s < kArMaxRanks; s++)
-        if (s < n) {
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const float q =
-                    unsigned(w[s][i] >> 32) == seq ? __uint_as_float(unsigned(w[s][i])) : ar_word(p + s * stride + i, seq);
-                v[i] = s == 0 ? q : __fadd_rn(v[i], q);
+                for (int i = 0; i < 4; i++)
+                    ld_relaxed_sys_v2u64(p + (s0 + s) * stride + 2 * i, w[s][2 * i], w[s][2 * i + 1]);
             }
-        }
+#pragma unroll
+        for (int s = 0; s < kArRound; s++)
+            if (s0 + s < n) {
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const float q = unsigned(w[s][i] >> 32) == seq ? __uint_as_float(unsigned(w[s][i]))
+                                                                   : ar_word(p + (s0 + s) * stride + i, seq);
+                    v[i] = s0 + s == 0 ? q : __fadd_rn(v[i], q);
+                }
+            }
+    }
 }
 
 // Thread 0 of every consumer CTA, first: this call's sequence number. The

@@ -131,7 +131,7 @@ extern "C" cpq_status cpq_mul_mat_noalloc(const cpq_tensor *w, const cpq_tensor 
     pa.m = int(m);
     pa.eps = 0.0f;
     pa.out = act;
-    cudaError_t e = launch(act_prep_kernel, dim3(unsigned((a.nbk + 7) / 8), unsigned(m)), dim3(256), 0, st, pa);
+    cudaError_t e = launch(act_prep_kernel<false>, dim3(unsigned((a.nbk + 7) / 8), unsigned(m)), dim3(256), 0, st, pa);
     if (e != cudaSuccess) return cuda_fail(e, "cpq_mul_mat_noalloc: act_prep launch");
     switch (m) {
     case 1: e = noalloc_launch_row<1>(a, smem, st); break;
