@@ -173,10 +173,14 @@ __device__ __forceinline__ bool act_rms_row(const float *xr, const float *rr, in
 
 // grid: (ceil(nbk / 8), m); block 256 = 8 warps, warp w quantizes block 8*blockIdx.x + w of token blockIdx.y
 // AR: the input's residual comes from an all-reduce channel (a.ar); the
-// instance without it carries none of that code, so it stays small enough
-// to share an SM with a GEMV CTA while it waits.
+// instance without it carries none of that code. Both stay small enough
+// (256 threads x at most 104 registers) to share an SM with a row-GEMV CTA
+// while they wait under programmatic dependent launch.
+#ifndef CPQ_ACT_AR_MAXNREG
+#define CPQ_ACT_AR_MAXNREG 104
+#endif
 template <bool AR>
-__global__ void __launch_bounds__(256, 1) act_prep_kernel(const ActPrepArgs a) {
+__global__ void __launch_bounds__(256, 1) __maxnreg__(AR ? CPQ_ACT_AR_MAXNREG : 104) act_prep_kernel(const ActPrepArgs a) {
     // Dependents (the row GEMV) may launch before this kernel even starts
     // waiting: they only prefetch weights until their own griddepcontrol.wait,
     // which still orders them after this kernel, and so they take each SM as

@@ -295,7 +295,10 @@ __device__ __forceinline__ void ld_relaxed_sys_v2u64(const uint64_t *p, uint64_t
 // are issued before any is looked at, so n ranks cost ceil(n / kArRound)
 // memory round trips, not n; a word without the expected sequence number is
 // then waited for on its own.
-constexpr int kArRound = 4;
+#ifndef CPQ_AR_ROUND
+#define CPQ_AR_ROUND 2
+#endif
+constexpr int kArRound = CPQ_AR_ROUND;
 __device__ __forceinline__ void ar_sum8(const uint64_t *p, int64_t stride, int n, unsigned seq, float (&v)[8]) {
     for (int s0 = 0; s0 < n; s0 += kArRound) {
         uint64_t w[kArRound][8];
