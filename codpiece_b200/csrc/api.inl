@@ -74,12 +74,36 @@ static bool pdl_enabled() {
     return on;
 }
 
+// Every kernel prefers the largest shared-memory carveout: the small kernels
+// of a decode chain then run under the same SM configuration as the GEMVs
+// they overlap with (a different split would keep them off an SM until its
+// GEMV CTA has left). Set once per kernel and device.
+#ifndef CPQ_CARVEOUT
+#define CPQ_CARVEOUT 1
+#endif
+static void prefer_max_shared(const void *fn) {
+#if CPQ_CARVEOUT
+    static std::mutex mu;
+    static std::unordered_map<const void *, uint64_t> done;  // kernel -> bit set of devices
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
+    std::lock_guard<std::mutex> lk(mu);
+    uint64_t &bits = done[fn];
+    if (bits & (uint64_t(1) << dev)) return;
+    bits |= uint64_t(1) << dev;
+    cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+#else
+    (void)fn;
+#endif
+}
+
 // Every kernel is launched with programmatic stream serialization allowed,
 // so its prologue can overlap the tail of the previous kernel on the stream;
 // each kernel calls griddepcontrol.wait before touching its inputs.
 template <typename... KArgs, typename... Args>
 static cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                           Args &&...args) {
+    prefer_max_shared(reinterpret_cast<const void *>(kern));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
