@@ -33,6 +33,7 @@ inside an NVTX range named "step" (ncu --nvtx --nvtx-include step/):
   decode_ffn   Q4_K mul_mat M=1 on config 2's gate and down shapes, 2 calls each
   prefill_512  Q4_K mul_mat M=512 on [17408 x 5120], 1 call
   stack        --steps replays of the captured stack decode step
+  head         Q6_K mul_mat on the head [151936 x 5120] at M = 1 and M = 8, 1 call each
 """
 from __future__ import annotations
 
@@ -295,6 +296,17 @@ def profile_case(args) -> int:
         mm.mul_mat(w, x)
         torch.cuda.synchronize()
         nvtx.range_pop()
+    elif args.profile == "head":
+        w = mm.synth_weights(mm.TYPE_Q6_K, 5120, 151936, seed=31)
+        xs = [torch.randn(m, 5120, device="cuda") for m in (1, 8)]
+        for x in xs:
+            mm.mul_mat(w, x)
+        torch.cuda.synchronize()
+        nvtx.range_push("step")
+        for x in xs:
+            mm.mul_mat(w, x)
+        torch.cuda.synchronize()
+        nvtx.range_pop()
     elif args.profile == "stack":
         from codpiece_b200 import stack as st
         from codpiece_b200 import tp
@@ -379,7 +391,7 @@ def main() -> int:
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-verify", action="store_true")
     ap.add_argument("--nccl", action="store_true", help="TP partial sums through NCCL instead of the fused allreduce")
-    ap.add_argument("--profile", default=None, choices=["decode_ffn", "prefill_512", "stack"])
+    ap.add_argument("--profile", default=None, choices=["decode_ffn", "prefill_512", "stack", "head"])
     args = ap.parse_args()
     if args.profile:
         return profile_case(args)

@@ -290,6 +290,56 @@ static cudaError_t launch_gemv(const GemvArgs &a, int mt, cudaStream_t st) {
 }
 
 constexpr int kGemvMaxTokens = 8;  // tokens per GEMV launch (dp4a kernels)
+constexpr int kSmemMax = 227 * 1024;  // dynamic shared memory a CTA may ask for on sm_100
+
+// Q6_K over whole row pairs (gemv_q6k.cuh): one weight, dense 16-byte aligned
+// rows, K a multiple of 1024 (a row pair is then a 16-byte multiple), an
+// even row count, and the activations of the token group in shared memory.
+static int q6r_mt(int mt) { return mt <= 2 ? mt : mt <= 4 ? 4 : 8; }  // the kernel instance for mt tokens
+
+static bool q6k_rows_ok(const GemvArgs &g, int mt) {
+    const int64_t nbk = g.k / kQK_K;
+    const int64_t n = g.row_start[1] - g.row_start[0];
+    return g.n_w == 1 && g.k % 1024 == 0 && n % 2 == 0 && n > 0 && g.rs == size_t(nbk) * kQ6K_Bytes &&
+           aligned(g.w[0], 16) && aligned(g.act.qs, 16) && aligned(g.act.d, 16) && aligned(g.act.bsums, 16) &&
+           mt <= kQ6rMaxTokens && q6r_smem_bytes(int(nbk), q6r_mt(mt)) <= kSmemMax;
+}
+
+template <int MT>
+static cudaError_t launch_q6k_rows_t(const Q6RowArgs &a, cudaStream_t st) {
+    auto kern = gemv_q6k_rows_kernel<MT>;
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    static std::atomic<int> set[kMaxDevices];
+    if (!set[dev].load(std::memory_order_relaxed)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        if (e != cudaSuccess) return e;
+        set[dev].store(1, std::memory_order_relaxed);
+    }
+    const int64_t pairs = a.n / 2;
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), (pairs + kQ6rWarps - 1) / kQ6rWarps));
+    return launch(kern, dim3(unsigned(grid)), dim3(kQ6rWarps * 32), size_t(q6r_smem_bytes(a.nbk, MT)), st, a);
+}
+
+static cudaError_t launch_q6k_rows(const GemvArgs &g, int mt, cudaStream_t st) {
+    Q6RowArgs a;
+    a.w = g.w[0];
+    a.y = g.y[0];
+    a.y_stride = g.y_stride[0];
+    a.n = g.row_start[1] - g.row_start[0];
+    a.nbk = int(g.k / kQK_K);
+    a.m = mt;
+    a.qs = g.act.qs;
+    a.d = g.act.d;
+    a.bsums = g.act.bsums;
+    switch (mt) {
+    case 1: return launch_q6k_rows_t<1>(a, st);
+    case 2: return launch_q6k_rows_t<2>(a, st);
+    case 3:
+    case 4: return launch_q6k_rows_t<4>(a, st);
+    default: return launch_q6k_rows_t<8>(a, st);
+    }
+}
 
 // Q4_K: fragment-order quantization, then the tensor-core GEMV per group of
 // up to 16 tokens.
@@ -427,7 +477,6 @@ static size_t frag_bytes(int64_t k, int mp) {
     return align_up(nbk * mp * 256, 256) + align_up(nbk * mp * 16, 256) + align_up(nbk * mp * 4, 256);
 }
 
-constexpr int kSmemMax = 227 * 1024;
 
 static int row_smem_bytes(int64_t k, int mt) {
     return kRowBarBytes + row_act_bytes(k, mt) + kRowRingBytes + row_red_bytes(mt);
@@ -745,7 +794,7 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
         g.act.bsums = reinterpret_cast<const int16_t *>(base + L.bs_off) + t0 * (s0.k / 16);
         for (int i = 0; i < n_w; i++) g.y[i] = a.y[i] + t0 * a.y_stride[i];
         switch (s0.wtype) {
-        case CPQ_TYPE_Q6_K: e = launch_gemv<FmtQ6K>(g, mt, st); break;
+        case CPQ_TYPE_Q6_K: e = q6k_rows_ok(g, mt) ? launch_q6k_rows(g, mt, st) : launch_gemv<FmtQ6K>(g, mt, st); break;
         default: e = launch_gemv<FmtQ8_0>(g, mt, st); break;
         }
         if (e != cudaSuccess) return cuda_fail(e, "gemv launch");

@@ -63,6 +63,14 @@ CASES = [
     (synth.Q6_K, 4099, 5120, 8),
     (synth.Q6_K, 5, 768, 2),
     (synth.Q6_K, 1, 256, 1),
+    # even N, K % 1024 == 0: the row-pair kernel (gemv_q6k.cuh), every token-count instance
+    (synth.Q6_K, 4098, 5120, 1),
+    (synth.Q6_K, 4098, 5120, 8),
+    (synth.Q6_K, 6, 1024, 3),
+    (synth.Q6_K, 2048, 2048, 5),
+    (synth.Q6_K, 302, 3072, 2),
+    (synth.Q6_K, 1000, 5120, 12),
+    (synth.Q6_K, 300, 1536, 1),  # K % 1024 != 0: the generic kernel
     (synth.Q8_0, 9, 96, 7),
     (synth.Q8_0, 1001, 2080, 1),
     (synth.Q4_K, 300, 2048, 40),
