@@ -343,17 +343,20 @@ static cudaError_t launch_q6k_rows(const GemvArgs &g, int mt, cudaStream_t st) {
 
 // Q4_K: fragment-order quantization, then the tensor-core GEMV per group of
 // up to 16 tokens.
-template <int NG>
+// SM: the activation image goes to shared memory (a.act_smem bytes after the ring).
+template <int NG, bool SM>
 static cudaError_t launch_q4k_mma_t(MmaArgs &a, cudaStream_t st) {
-    auto kern = gemv_q4k_mma_kernel<NG>;
+    auto kern = gemv_q4k_mma_kernel<NG, SM>;
+    const int smem = kMmaSmem + (SM ? a.act_smem : 0);
     const int dev = current_device();
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     static std::atomic<int> occ[kMaxDevices];
     int bpm = occ[dev].load(std::memory_order_relaxed);
     if (bpm == 0) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaSmem);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             SM ? int(227 * 1024) : kMmaSmem);
         if (e != cudaSuccess) return e;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bpm, kern, kMmaWarps * 32, kMmaSmem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bpm, kern, kMmaWarps * 32, SM ? 227 * 1024 : kMmaSmem);
         if (e != cudaSuccess) return e;
         if (bpm < 1) bpm = 1;
         occ[dev].store(bpm, std::memory_order_relaxed);
@@ -362,7 +365,7 @@ static cudaError_t launch_q4k_mma_t(MmaArgs &a, cudaStream_t st) {
     const int64_t cap = std::min<int64_t>(int64_t(sm_count(dev)) * bpm * kMmaWarps, int64_t(kWsMaxWarps));
     a.n_warps = std::max<int64_t>(1, std::min<int64_t>(cap, T));
     const int64_t grid = (a.n_warps + kMmaWarps - 1) / kMmaWarps;
-    return launch(kern, dim3(unsigned(grid)), dim3(kMmaWarps * 32), kMmaSmem, st, a);
+    return launch(kern, dim3(unsigned(grid)), dim3(kMmaWarps * 32), size_t(smem), st, a);
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no
@@ -613,7 +616,13 @@ static cpq_status run_q4k_mma(const GemvArgs &g, const float *x, int64_t x_strid
         a.act.d = d;
         a.act.mp = mp;
         for (int i = 0; i < g.n_w; i++) a.y[i] = g.y[i] + t0 * g.y_stride[i];
-        e = mt <= 8 ? launch_q4k_mma_t<1>(a, st) : launch_q4k_mma_t<2>(a, st);
+        // the image in shared memory when it fits beside the ring (M <= 8 and K up to about 7.7K)
+        const size_t img = size_t(nbk) * mp * (256 + 16) + align_up(size_t(nbk) * mp * 4, 16);
+        a.act_smem = (mp == 8 && size_t(kMmaSmem) + img <= size_t(227 * 1024)) ? int(img) : 0;
+        if (mt <= 8)
+            e = a.act_smem ? launch_q4k_mma_t<1, true>(a, st) : launch_q4k_mma_t<1, false>(a, st);
+        else
+            e = launch_q4k_mma_t<2, false>(a, st);
         if (e != cudaSuccess) return cuda_fail(e, "q4_K gemv launch");
     }
     return CPQ_SUCCESS;

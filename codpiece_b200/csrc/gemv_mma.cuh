@@ -50,7 +50,7 @@ constexpr int kMmaStages = CPQ_MMA_STAGES;
 constexpr int kMmaRows = 16;
 constexpr int kMmaPitch = kMmaSB * kQ4K_Bytes;
 constexpr int kMmaStageBytes = kMmaRows * kMmaPitch;
-constexpr int kMmaBarBytes = 128 * ((kMmaWarps * kMmaStages * 8 + 127) / 128);
+constexpr int kMmaBarBytes = 128 * ((kMmaWarps * kMmaStages * 8 + 8 + 127) / 128);  // + the activation barrier
 constexpr int kMmaSmem = kMmaBarBytes + kMmaWarps * kMmaStages * kMmaStageBytes;
 constexpr int kMmaMaxTokens = 16;
 static_assert(kMmaPitch % 128 == 32, "fragment loads of rows gid..gid+3 must hit distinct bank groups");
@@ -79,6 +79,7 @@ struct alignas(64) MmaArgs {
     int m;                   // tokens (1..16)
     ActFrag act;
     int64_t n_warps;         // G: warps taking part (<= iterations, so none is idle)
+    int act_smem;            // > 0: bytes of the activation image, copied into shared memory after the ring
     float *partials;         // [warp][2 segments][16 rows][16 tokens]
     int *counters;           // [row block], zero between calls
 };
@@ -141,7 +142,8 @@ struct ActRegs {
     float2 dx[NG];              // Q8_K scales of output tokens ng*8+2*tig, +1
 };
 
-template <int NG>
+// SM: the image is in shared memory (plain loads) rather than global (read-only path).
+template <int NG, bool SM>
 __device__ __forceinline__ void load_act(const ActFrag &act, int kb, int m, int gid, int tig, ActRegs<NG> &r) {
 #pragma unroll
     for (int ng = 0; ng < NG; ng++) {
@@ -150,16 +152,19 @@ __device__ __forceinline__ void load_act(const ActFrag &act, int kb, int m, int 
         const int4 *p = reinterpret_cast<const int4 *>(act.qs + bt * 256 + tig * 64);
 #pragma unroll
         for (int v = 0; v < 4; v++) {
-            const int4 q = live ? ldg_nc_v4(p + v) : make_int4(0, 0, 0, 0);
+            const int4 q = live ? (SM ? p[v] : ldg_nc_v4(p + v)) : make_int4(0, 0, 0, 0);
             r.bw[ng][4 * v + 0] = q.x;
             r.bw[ng][4 * v + 1] = q.y;
             r.bw[ng][4 * v + 2] = q.z;
             r.bw[ng][4 * v + 3] = q.w;
         }
-        const int4 b = (live && tig < 2) ? ldg_nc_v4(act.bs + bt * 16) : make_int4(0, 0, 0, 0);
+        const int4 b = (live && tig < 2)
+                           ? (SM ? *reinterpret_cast<const int4 *>(act.bs + bt * 16) : ldg_nc_v4(act.bs + bt * 16))
+                           : make_int4(0, 0, 0, 0);
         r.blo[ng] = tig == 0 ? uint32_t(b.x) : (tig == 1 ? uint32_t(b.y) : 0u);
         r.bhi[ng] = tig == 0 ? uint32_t(b.z) : (tig == 1 ? uint32_t(b.w) : 0u);
-        r.dx[ng] = __ldg(reinterpret_cast<const float2 *>(act.d + size_t(kb) * act.mp + ng * 8 + 2 * tig));
+        const float2 *dp = reinterpret_cast<const float2 *>(act.d + size_t(kb) * act.mp + ng * 8 + 2 * tig);
+        r.dx[ng] = SM ? *dp : __ldg(dp);
     }
 }
 
@@ -226,19 +231,24 @@ __device__ __forceinline__ void q4k_superblock(const uint8_t *p0, const uint8_t 
     }
 }
 
-template <int NG>  // token groups of 8 (1: M <= 8, 2: M <= 16)
+// SM: the activation image is copied into shared memory (a.act_smem bytes,
+// after the ring) once per CTA, so the per-superblock fragment loads do not
+// wait on L2.
+template <int NG, bool SM>  // token groups of 8 (1: M <= 8, 2: M <= 16)
 __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __grid_constant__ MmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gid = lane >> 2, tig = lane & 3;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * kMmaStages;
+    uint64_t *act_bar = reinterpret_cast<uint64_t *>(smem) + kMmaWarps * kMmaStages;
     uint8_t *ring = smem + kMmaBarBytes + warp * kMmaStages * kMmaStageBytes;
     if (lane == 0) {
 #pragma unroll
         for (int s = 0; s < kMmaStages; s++) mbar_init(&bars[s], 1);
+        if (SM && warp == 0) mbar_init(act_bar, 1);
         fence_mbar_init();
     }
-    __syncwarp();
+    __syncthreads();
 
     const int nbk = a.nbk;
     const int64_t T = a.mb_start[a.n_w] * nbk;
@@ -259,7 +269,9 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __gr
     // producer cursor
     int64_t p_it = it_begin, p_mb = it_begin / nbk;
     int p_kb = int(it_begin - p_mb * nbk);
+    int n_issued = 0;  // stages issued before the activation wait
     auto issue = [&](int slot) {
+        n_issued++;
         const int n = int(min(int64_t(min(kMmaSB, nbk - p_kb)), it_end - p_it));
         if (lane == 0) {
             const int wi = weight_of(p_mb);
@@ -279,6 +291,27 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __gr
 
     pdl_wait();
     pdl_launch_dependents();
+    ActFrag act = a.act;
+    if (SM) {
+        // the activation image (quants, split 32-sums, scales) into shared memory after the ring
+        uint8_t *as = smem + kMmaSmem;
+        const uint32_t qb = uint32_t(nbk) * uint32_t(act.mp) * 256u, bb = uint32_t(nbk) * uint32_t(act.mp) * 16u;
+        const uint32_t db = uint32_t(align_up(size_t(nbk) * act.mp * 4, 16));
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(act_bar, qb + bb + db);
+            bulk_g2s(as, a.act.qs, qb, act_bar);
+            bulk_g2s(as + qb, a.act.bs, bb, act_bar);
+            bulk_g2s(as + qb + bb, a.act.d, db, act_bar);
+        }
+        if (!mbar_wait_bounded(act_bar, 0)) {
+            // error recorded in the device word: wait (bounded) for this warp's weight copies, then leave
+            for (int k2 = 0; k2 < n_issued; k2++) mbar_wait_bounded(&bars[k2], 0);
+            return;
+        }
+        act.qs = reinterpret_cast<const int8_t *>(as);
+        act.bs = as + qb;
+        act.d = reinterpret_cast<const float *>(as + qb + bb);
+    }
 
     float acc[NG][4];
 #pragma unroll
@@ -290,7 +323,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __gr
     int c_kb = int(it_begin - c_mb * nbk);
     int64_t seg_start = it_begin;
     ActRegs<NG> ra, rb;
-    load_act<NG>(a.act, c_kb, a.m, gid, tig, ra);
+    load_act<NG, SM>(act, c_kb, a.m, gid, tig, ra);
     int slot = 0;
     uint32_t phase = 0;
     while (c_it < it_end) {
@@ -313,13 +346,13 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __gr
         {
             int kn = c_kb + 1;
             if (kn == nbk) kn = 0;
-            load_act<NG>(a.act, kn, a.m, gid, tig, rb);
+            load_act<NG, SM>(act, kn, a.m, gid, tig, rb);
             q4k_superblock<NG>(p0, p1, ra, tig, acc);
         }
         if (n == 2) {
             int kn = c_kb + 2;
             if (kn >= nbk) kn -= nbk;
-            load_act<NG>(a.act, kn, a.m, gid, tig, ra);
+            load_act<NG, SM>(act, kn, a.m, gid, tig, ra);
             q4k_superblock<NG>(p0 + kQ4K_Bytes, p1 + kQ4K_Bytes, rb, tig, acc);
         } else {
             ra = rb;
