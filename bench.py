@@ -243,6 +243,75 @@ def prefill_roofline(torch, mm, reps: int = 10):
             "achieved_is": "FLOP-weighted over the four configs[3] cases", "best": best, "cases": cases}
 
 
+def _time_graph(torch, calls, reps: int = 10):
+    """Average duration of one of `calls` (closures that enqueue one mul_mat), replayed in a CUDA graph."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for c in calls:
+            c()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for c in calls:
+            c()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for _ in range(reps):
+        g.replay()
+    e1.record(cur)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / (reps * len(calls))
+
+
+def small_configs(torch, mm):
+    """configs[0] (Q8_0 [5120x5120] mat-vec, M = 1) and configs[2] (one layer's Q4_K q/k/v/o and the Q6_K
+    head [151936x5120] at M = 2, 4, 8, 16): weight GB/s of each mul_mat, rotating weights larger than L2."""
+    hbm, kind = peaks()
+    out = {"peak_gbs": hbm, "peak_kind": kind}
+    q8 = [mm.synth_weights(mm.TYPE_Q8_0, 5120, 5120, seed=8000 + i) for i in range(24)]  # 668 MB
+    x1 = torch.randn(1, 5120, device="cuda")
+    y1 = torch.empty(1, 5120, device="cuda")
+    us = _time_graph(torch, [lambda w=w: mm.mul_mat(w, x1, out=y1) for w in q8])
+    out["config1_q8_0_m1"] = {"us": round(us, 2), "GBs": round(q8[0].nbytes / us / 1e3, 1),
+                              "frac": round(q8[0].nbytes / us / 1e3 / hbm, 4)}
+    del q8
+    sets = []
+    for sidx in range(6):  # 6 x 41 MB > L2
+        sd = 8100 + 10 * sidx
+        sets.append((mm.synth_weights(mm.TYPE_Q4_K, 5120, 6144, seed=sd),
+                     mm.synth_weights(mm.TYPE_Q4_K, 5120, 1024, seed=sd + 1),
+                     mm.synth_weights(mm.TYPE_Q4_K, 5120, 1024, seed=sd + 2),
+                     mm.synth_weights(mm.TYPE_Q4_K, 6144, 5120, seed=sd + 3)))
+    head = mm.synth_weights(mm.TYPE_Q6_K, 5120, 151936, seed=8200)
+    attn_bytes = sum(w.nbytes for w in sets[0])
+    per_m = []
+    for m in (2, 4, 8, 16):
+        x = torch.randn(m, 5120, device="cuda")
+        xo = torch.randn(m, 6144, device="cuda")
+        outs = [torch.empty(m, n, device="cuda") for n in (6144, 1024, 1024)]
+        yo = torch.empty(m, 5120, device="cuda")
+        calls = []
+        for q, k, v, o in sets:
+            calls.append(lambda q=q, k=k, v=v: mm.mul_mat_multi([q, k, v], x, outs))
+            calls.append(lambda o=o: mm.mul_mat(o, xo, out=yo))
+        us_pair = _time_graph(torch, calls) * 2  # one q/k/v call + one o call
+        yh = torch.empty(m, 151936, device="cuda")
+        us_head = _time_graph(torch, [lambda: mm.mul_mat(head, x, out=yh)], reps=5)
+        per_m.append({"m": m, "attn_set_us": round(us_pair, 2), "attn_GBs": round(attn_bytes / us_pair / 1e3, 1),
+                      "head_us": round(us_head, 1), "head_GBs": round(head.nbytes / us_head / 1e3, 1),
+                      "head_frac": round(head.nbytes / us_head / 1e3 / hbm, 4)})
+        del x, xo, outs, yo, yh
+    out["config3_verify_small_m"] = per_m
+    return out
+
+
 def verify_step(torch, st, tp, layers: int, m: int = 8, steps: int = 10):
     """configs[4]'s verify step: the same stack at M = 8 tokens (MMA GEMVs, NCCL-free at TP1)."""
     stack = st.Stack(tp.HP_BENCH_27B, layers, 0, 1, None, m=m, seed=0)
@@ -390,6 +459,7 @@ def main() -> int:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-verify", action="store_true")
+    ap.add_argument("--no-small", action="store_true", help="skip the configs[0] / configs[2] lines")
     ap.add_argument("--nccl", action="store_true", help="TP partial sums through NCCL instead of the fused allreduce")
     ap.add_argument("--profile", default=None, choices=["decode_ffn", "prefill_512", "stack", "head"])
     args = ap.parse_args()
@@ -507,10 +577,13 @@ def main() -> int:
     launches = stack.launches_per_step() * args.steps
 
     roof = prefill = verify = None
+    small = None
     if rank == 0:
         roof = kernel_roofline(torch, mm, cur)
         if not args.no_prefill:
             prefill = prefill_roofline(torch, mm)
+        if world == 1 and not args.no_small:
+            small = small_configs(torch, mm)
     barrier()
     if world == 1 and not args.no_verify:
         verify = verify_step(torch, st, tp, args.layers)
@@ -553,6 +626,7 @@ def main() -> int:
         "cpu_baseline": cpu,
         "prefill": prefill,
         "verify": verify,
+        "small_configs": small,
     }
     print(json.dumps(line), flush=True)
     return 0

@@ -321,6 +321,52 @@ static cudaError_t launch_q6k_rows_t(const Q6RowArgs &a, cudaStream_t st) {
     return launch(kern, dim3(unsigned(grid)), dim3(kQ6rWarps * 32), size_t(q6r_smem_bytes(a.nbk, MT)), st, a);
 }
 
+// Q8_0 over whole row pairs (gemv_q6k.cuh): one weight, dense 16-byte aligned
+// rows, K a multiple of 256, an even row count.
+static bool q8_rows_ok(const GemvArgs &g, int mt) {
+    const int64_t nb = g.k / kQK8_0;
+    const int64_t n = g.row_start[1] - g.row_start[0];
+    const int mr = mt <= 2 ? mt : mt <= 4 ? 4 : 8;
+    return g.n_w == 1 && g.k % 256 == 0 && n % 2 == 0 && n > 0 && g.rs == size_t(nb) * kQ8_0_Bytes &&
+           aligned(g.w[0], 16) && aligned(g.act.qs, 16) && aligned(g.act.d, 16) && mt <= 8 &&
+           q8r_smem_bytes(int(nb), mr) <= kSmemMax;
+}
+
+template <int MT>
+static cudaError_t launch_q8_rows_t(const Q8RowArgs &a, cudaStream_t st) {
+    auto kern = gemv_q8_0_rows_kernel<MT>;
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    static std::atomic<int> set[kMaxDevices];
+    if (!set[dev].load(std::memory_order_relaxed)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        if (e != cudaSuccess) return e;
+        set[dev].store(1, std::memory_order_relaxed);
+    }
+    const int64_t pairs = a.n / 2;
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), (pairs + kQ8rWarps - 1) / kQ8rWarps));
+    return launch(kern, dim3(unsigned(grid)), dim3(kQ8rWarps * 32), size_t(q8r_smem_bytes(a.nb, MT)), st, a);
+}
+
+static cudaError_t launch_q8_rows(const GemvArgs &g, int mt, cudaStream_t st) {
+    Q8RowArgs a;
+    a.w = g.w[0];
+    a.y = g.y[0];
+    a.y_stride = g.y_stride[0];
+    a.n = g.row_start[1] - g.row_start[0];
+    a.nb = int(g.k / kQK8_0);
+    a.m = mt;
+    a.qs = g.act.qs;
+    a.d = g.act.d;
+    switch (mt) {
+    case 1: return launch_q8_rows_t<1>(a, st);
+    case 2: return launch_q8_rows_t<2>(a, st);
+    case 3:
+    case 4: return launch_q8_rows_t<4>(a, st);
+    default: return launch_q8_rows_t<8>(a, st);
+    }
+}
+
 static cudaError_t launch_q6k_rows(const GemvArgs &g, int mt, cudaStream_t st) {
     Q6RowArgs a;
     a.w = g.w[0];
@@ -804,7 +850,7 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
         for (int i = 0; i < n_w; i++) g.y[i] = a.y[i] + t0 * a.y_stride[i];
         switch (s0.wtype) {
         case CPQ_TYPE_Q6_K: e = q6k_rows_ok(g, mt) ? launch_q6k_rows(g, mt, st) : launch_gemv<FmtQ6K>(g, mt, st); break;
-        default: e = launch_gemv<FmtQ8_0>(g, mt, st); break;
+        default: e = q8_rows_ok(g, mt) ? launch_q8_rows(g, mt, st) : launch_gemv<FmtQ8_0>(g, mt, st); break;
         }
         if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
     }

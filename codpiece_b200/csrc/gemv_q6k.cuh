@@ -222,4 +222,151 @@ __global__ void __launch_bounds__(kQ6rWarps * 32, 1) gemv_q6k_rows_kernel(const 
     }
 }
 
+
+// ---- Q8_0 over whole row pairs -------------------------------------------
+//
+// The same structure for Q8_0 (ggml_vec_dot_q8_0_q8_0: 32-element blocks,
+// integer dot of the quants, times d_w * d_x in fp32 per block): a stage is
+// two whole rows, 2 * K/32 * 34 bytes (a multiple of 16 when K is a multiple
+// of 128), one bulk copy; an item is one block of one row; the Q8_0
+// activations (quants and scales) of all MT tokens are in shared memory, the
+// quants at 16-byte slot s ^ ((s >> 3) & 1), which puts the two 16-byte loads
+// of the 8 lanes of a quarter warp (8 consecutive blocks) on 8 different bank
+// groups.
+
+constexpr int kQ8rWarps = 8;
+
+struct Q8RowArgs {
+    const uint8_t *w;      // [n rows][nb * 34 B], dense, 16-byte aligned
+    float *y;
+    int64_t y_stride;
+    int64_t n;             // rows (even)
+    int nb;                // 32-element blocks per row (a multiple of 8: token rows are then
+                           // 16-slot multiples, which the swizzle leaves alone)
+    int m;
+    const int8_t *qs;      // Q8_0 quants [m][K]
+    const float *d;        // Q8_0 scales [m][nb] (fp16 widened)
+};
+
+__host__ __device__ constexpr int q8r_stage_bytes(int nb) { return 2 * nb * kQ8_0_Bytes; }
+__host__ __device__ constexpr int q8r_bar_bytes() { return 128 * ((kQ8rWarps * 3 * 8 + 8 + 127) / 128); }
+__host__ __device__ constexpr int q8r_act_bytes(int nb, int m) {
+    return int(align_up(size_t(m) * nb * kQK8_0, 16) + align_up(size_t(m) * nb * 4, 16));
+}
+__host__ __device__ constexpr int q8r_stages(int) { return 2; }  // two 10.9 KB stages per warp at K = 5120
+// + 16 bytes: the last block's quants are read with aligned 4-byte loads that reach 2 bytes past it
+__host__ __device__ constexpr int q8r_smem_bytes(int nb, int m) {
+    return q8r_bar_bytes() + q8r_act_bytes(nb, m) + kQ8rWarps * q8r_stages(m) * q8r_stage_bytes(nb) + 16;
+}
+__device__ __forceinline__ int q8r_swz(int s) { return s ^ ((s >> 3) & 1); }
+
+template <int MT>
+__global__ void __launch_bounds__(kQ8rWarps * 32, 1) gemv_q8_0_rows_kernel(const __grid_constant__ Q8RowArgs a) {
+    constexpr int S = q8r_stages(MT);
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = a.nb;
+    const int64_t k = int64_t(nb) * kQK8_0;
+    const int sb = q8r_stage_bytes(nb);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * S;
+    uint64_t *act_bar = reinterpret_cast<uint64_t *>(smem) + kQ8rWarps * 3;
+    int8_t *xq = reinterpret_cast<int8_t *>(smem + q8r_bar_bytes());
+    float *xd = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(xq) + align_up(size_t(MT) * k, 16));
+    uint8_t *ring = smem + q8r_bar_bytes() + q8r_act_bytes(nb, MT) + warp * S * sb;
+    const uint32_t qs_bytes = uint32_t(align_up(size_t(a.m) * k, 16));
+    const uint32_t d_bytes = uint32_t(align_up(size_t(a.m) * nb * 4, 16));
+    if (lane == 0) {
+#pragma unroll
+        for (int s = 0; s < S; s++) mbar_init(&bars[s], 1);
+        if (warp == 0) mbar_init(act_bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    const int64_t npairs = a.n / 2;
+    const int64_t G = int64_t(gridDim.x) * kQ8rWarps;
+    const int64_t g = int64_t(blockIdx.x) * kQ8rWarps + warp;
+    const int64_t p_begin = g * npairs / G, p_end = (g + 1) * npairs / G;
+    const uint64_t policy = l2_policy_evict_first();
+    int64_t p_issue = p_begin;
+    auto issue = [&](int slot) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&bars[slot], uint32_t(sb));
+            bulk_g2s_stream(ring + slot * sb, a.w + size_t(p_issue) * sb, uint32_t(sb), &bars[slot], policy);
+        }
+        p_issue++;
+    };
+    for (int s = 0; s < S && p_issue < p_end; s++) issue(s);
+
+    pdl_wait();
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(act_bar, d_bytes);
+        bulk_g2s(xd, a.d, d_bytes, act_bar);
+    }
+    {
+        const int4 *src = reinterpret_cast<const int4 *>(a.qs);
+        int4 *dst = reinterpret_cast<int4 *>(xq);
+        const int nslots = int(qs_bytes >> 4);
+        for (int s = threadIdx.x; s < nslots; s += blockDim.x) dst[q8r_swz(s)] = __ldcg(src + s);
+    }
+    __syncthreads();
+    const int64_t pre = p_issue - p_begin;
+    if (!mbar_wait_bounded(act_bar, 0)) {
+        for (int64_t j = 0; j < pre; j++) mbar_wait_bounded(&bars[j], 0);
+        return;
+    }
+    pdl_launch_dependents();
+
+    const int items = 2 * nb;
+    const int tstride = int(k >> 4);  // slots per token row (a multiple of 8: the swizzle leaves it alone)
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int64_t pr = p_begin; pr < p_end; pr++) {
+        if (!mbar_wait_bounded(&bars[slot], phase)) {
+            for (int k2 = 1; k2 < S && p_issue > pr + k2; k2++)
+                mbar_wait_bounded(&bars[(slot + k2) % S], phase ^ uint32_t(slot + k2 >= S));
+            return;
+        }
+        const uint8_t *st = ring + slot * sb;
+        float acc0[MT], acc1[MT];
+#pragma unroll
+        for (int t = 0; t < MT; t++) acc0[t] = acc1[t] = 0.0f;
+        for (int it = lane; it < items; it += 32) {
+            const int row = it >= nb;
+            const int b = it - row * nb;
+            const uint8_t *blk = st + row * (nb * kQ8_0_Bytes) + b * kQ8_0_Bytes;
+            const uint16_t dbits = uint16_t(blk[0]) | uint16_t(uint16_t(blk[1]) << 8);
+            const float dw = half_bits_to_float(dbits);
+            const uint4 q0 = lds16_a2(blk + 2), q1 = lds16_a2(blk + 18);
+            const int4 *x0p = reinterpret_cast<const int4 *>(xq) + q8r_swz(2 * b);
+            const int4 *x1p = reinterpret_cast<const int4 *>(xq) + q8r_swz(2 * b + 1);
+#pragma unroll
+            for (int t = 0; t < MT; t++) {
+                if (t >= a.m) break;
+                const int4 x0 = x0p[t * tstride], x1 = x1p[t * tstride];
+                int dot = __dp4a(int(q0.x), x0.x, __dp4a(int(q0.y), x0.y, __dp4a(int(q0.z), x0.z, __dp4a(int(q0.w), x0.w, 0))));
+                dot = __dp4a(int(q1.x), x1.x, __dp4a(int(q1.y), x1.y, __dp4a(int(q1.z), x1.z, __dp4a(int(q1.w), x1.w, dot))));
+                const float v = float(dot) * (dw * xd[t * nb + b]);
+                if (row) acc1[t] += v;
+                else acc0[t] += v;
+            }
+        }
+        __syncwarp();
+        if (p_issue < p_end) issue(slot);
+#pragma unroll
+        for (int t = 0; t < MT; t++) {
+            if (t >= a.m) break;
+            const float v0 = warp_sum(acc0[t]), v1 = warp_sum(acc1[t]);
+            if (lane == 0) {
+                a.y[size_t(t) * a.y_stride + 2 * pr] = v0;
+                a.y[size_t(t) * a.y_stride + 2 * pr + 1] = v1;
+            }
+        }
+        if (++slot == S) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    }
+}
+
 }  // namespace cpq

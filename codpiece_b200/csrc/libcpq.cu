@@ -4,7 +4,7 @@
 // relocatable device code. Parts:
 //   quantize.cuh     activation re-quantization (Q8_K, Q8_0), bit-exact
 //   gemv.cuh         small-M fused dequant GEMV/GEMM, dp4a (Q6_K, Q8_0)
-//   gemv_q6k.cuh     Q6_K small-M GEMV over whole row pairs (the LM head)
+//   gemv_q6k.cuh     Q6_K and Q8_0 small-M GEMVs over whole row pairs (LM head, Q8_0 trunk)
 //   q8k_block.cuh    the Q8_K block quantizer shared by every Q8_K producer
 //   gemv_mma.cuh     Q4_K verify GEMM (M 4..16) on int8 mma tiles, stream-K
 //   act_prep.cuh     decode activation image: fused rms/swiglu prologue + Q8_K

@@ -73,6 +73,11 @@ CASES = [
     (synth.Q6_K, 300, 1536, 1),  # K % 1024 != 0: the generic kernel
     (synth.Q8_0, 9, 96, 7),
     (synth.Q8_0, 1001, 2080, 1),
+    # even N, K % 256 == 0: the Q8_0 row-pair kernel (gemv_q6k.cuh); config 1's shape first
+    (synth.Q8_0, 5120, 5120, 1),
+    (synth.Q8_0, 1002, 2048, 3),
+    (synth.Q8_0, 64, 256, 8),
+    (synth.Q8_0, 1000, 5120, 12),
     (synth.Q4_K, 300, 2048, 40),
 ]
 
