@@ -89,7 +89,12 @@ size_t cpq_mul_mat_workspace_size(const cpq_tensor *w, const cpq_tensor *x);
  * anything. Uses the workspace from cpq_init on the current device. */
 cpq_status cpq_mul_mat(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *y, void *stream);
 
-/* Same, with a caller-provided device workspace (e.g. from ggml-cuda's pool). */
+/* Same, with a caller-provided device workspace: one persistent buffer per
+ * device (at least cpq_mul_mat_workspace_size bytes, 256-byte aligned),
+ * zeroed once before its first use and used by no one else. It keeps the
+ * stream-K counters and the decode GEMV's hand-off words between calls (both
+ * zero whenever no call is running), so it must not be a fresh allocation
+ * from a shared memory pool on every call. */
 cpq_status cpq_mul_mat_ws(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *y, void *workspace,
                           size_t workspace_bytes, void *stream);
 
