@@ -25,7 +25,8 @@ def rms_norm(x: np.ndarray, eps: float = 1e-6) -> np.ndarray:
 
 def silu_mul(g: np.ndarray, u: np.ndarray) -> np.ndarray:
     g = g.astype(np.float32)
-    return ((g / (np.float32(1.0) + np.exp(-g))) * u).astype(np.float32)
+    with np.errstate(over="ignore"):  # exp(-g) = inf for g << 0 gives silu = 0, as in float arithmetic
+        return ((g / (np.float32(1.0) + np.exp(-g))) * u).astype(np.float32)
 
 
 def layer_step(h: np.ndarray, lw: dict, k: int, nthreads: int = 0) -> np.ndarray:
