@@ -1,11 +1,10 @@
 // noalloc.inl — cpq_mul_mat_noalloc: the Q4_K decode GEMV with static scratch.
 //
 // Some callers cannot allocate device memory at the moment they need a
-// product: code running while a CUDA graph is being captured (an allocation
-// there would break or be baked into the capture), host engines that hand
-// all device memory out through their own arena and forbid the library from
-// touching cudaMalloc, and latency-critical threads that must not hit the
-// implicit device synchronization a cudaMalloc/cudaFree can cause. For them
+// product: host engines that hand all device memory out through their own
+// arena and forbid the library from calling cudaMalloc, and latency-critical
+// threads that must not take the implicit device synchronization a
+// cudaMalloc/cudaFree can cause. For them
 // this entry point runs the decode GEMV (gemv_row.cuh, unchanged) with every
 // byte of its scratch — the quantized activation image and the tail-cut
 // words the CTAs hand each other — in one file-scope device array that is
@@ -32,7 +31,7 @@ constexpr int kNoAllocMaxTokens = kRowMaxTokens;
 constexpr int64_t kNoAllocMaxCtas = 148;  // CTAs given tail-cut slots (larger parts run on 148 SMs)
 constexpr size_t kNoAllocPieceBytes = size_t(kNoAllocMaxCtas) * kRowWarps * kPieceWords * sizeof(uint64_t);
 constexpr size_t kNoAllocActBytes = align_up(size_t(row_act_bytes(kNoAllocMaxK, kNoAllocMaxTokens)), 256);
-constexpr size_t kNoAllocBytes = kNoAllocPieceBytes + kNoAllocActBytes;  // ~1.4 MB
+constexpr size_t kNoAllocBytes = kNoAllocPieceBytes + kNoAllocActBytes;  // 1,318,400 B (about 1.3 MB)
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 

@@ -130,11 +130,11 @@ cpq_status cpq_mul_mat_fused(const cpq_tensor *const *w, cpq_tensor *const *y, i
                              const cpq_prologue *pro, void *stream);
 
 /* No counterpart in the reference: an entry point for callers that cannot
- * allocate device memory when they run the product (inside a CUDA graph
- * capture, under a host engine that owns every device allocation, or on a
- * thread that must not take the implicit device synchronization of
- * cudaMalloc/cudaFree). Same result as cpq_mul_mat, but all scratch lives in
- * one static device array of about 2.5 MB that the library reserves on every
+ * allocate device memory when they run the product (under a host engine that
+ * owns every device allocation, or on a thread that must not take the
+ * implicit device synchronization of cudaMalloc/cudaFree). Same result as
+ * cpq_mul_mat, but all scratch lives in one static device array of about
+ * 1.3 MB that the library reserves on every
  * GPU that loads it, held until the process exits; no cudaMalloc, no
  * cudaFree, no cpq_init needed. Limits: Q4_K weights only, M <= 3 tokens,
  * K <= 32768, N <= 262144 rows; anything larger returns CPQ_ERR_UNSUPPORTED

@@ -1,8 +1,8 @@
 """cpq_mul_mat_noalloc: the entry point for callers that cannot allocate.
 
-Callers that run the product while a CUDA graph is being captured, inside a
-host engine that owns all device memory, or on a thread that must not take
-cudaMalloc's implicit synchronization, call cpq_mul_mat_noalloc: the same
+Callers that run the product inside a host engine that owns all device
+memory, or on a thread that must not take cudaMalloc's implicit device
+synchronization, call cpq_mul_mat_noalloc: the same
 Q4_K decode product as cpq_mul_mat, with its scratch in a static device array
 the library reserves at load time instead of a workspace. These checks call
 it through the C ABI, twice in a row (the array keeps the previous call's
