@@ -23,6 +23,11 @@ exactly BASELINE config 2's Q4_K mat-vec shapes, 64 times over.
              at M = 512 and 2048 for both FFN shapes, TFLOP/s through
              mul_mat (activation pre-pass included) against
              MEASURED_PEAKS.json bf16_tflops
+  verify     the same 64-layer stack stepping M = 8 tokens (the speculative
+             verify batch of configs[4]), 1 GPU
+  small_configs  configs[0] (Q8_0 [5120 x 5120] mat-vec, M = 1) and configs[2]
+             (one layer's q/k/v/o and the Q6_K head at M = 2, 4, 8, 16):
+             weight GB/s of each mul_mat on rotating weights larger than L2
 
 --impl reference times the reference's CPU path for this operator (the
 oracle restatement: ggml itself is not available) on a bounded sample of the
