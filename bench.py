@@ -4,8 +4,9 @@
 Workload (every N): the 27B-shaped stack of BASELINE config 5 --
 64 layers of Q4_K q/k/v/o/gate/up/down (hidden 5120, q 6144, kv 1024,
 FFN 17408) plus a mirrored Q6_K head over vocab 151936 -- decoding M = 1
-token per step, tensor-parallel over N GPUs (one process per GPU, NCCL
-allreduce after every row-parallel projection). Its FFN projections are
+token per step, tensor-parallel over N GPUs (one process per GPU; the
+row-parallel partial sums are all-reduced through the fused NVLink channel,
+or through NCCL with --nccl). Its FFN projections are
 exactly BASELINE config 2's Q4_K mat-vec shapes, 64 times over.
 
   value      aggregate weight GB/s = weight bytes all ranks stream per step /
@@ -145,8 +146,6 @@ def traffic_from_profiles():
 
 def cpu_baseline(seconds: float = 10.0):
     """Oracle on config 2's three Q4_K matrices at M = 1, all host threads."""
-    import numpy as np
-
     from codpiece_b200 import synth
     from oracle import cpq_oracle as O
 
@@ -167,7 +166,6 @@ def cpu_baseline(seconds: float = 10.0):
             "sample": f"config 2 Q4_K gate/up/down [17408x5120, 17408x5120, 5120x17408] at M=1, {reps} passes "
                       f"({dt:.1f} s) on {nthreads} threads; restated ggml-cpu semantics (AVX2 integer dots, "
                       f"OpenMP over rows)"}
-    del np
 
 
 def kernel_roofline(torch, mm, stream, sets: int = 4, reps: int = 20):
