@@ -573,9 +573,6 @@ static cpq_status run_q4k_row(const GemvArgs &g, const float *x, int64_t x_strid
             if (rc) return rc;
         }
     }
-    if (a.mb_start[g.n_w] > int64_t(kWsCounters))
-        return fail(CPQ_ERR_UNSUPPORTED, "too many row blocks (%lld) for the workspace counters",
-                    (long long)a.mb_start[g.n_w]);
     uint8_t *act = ws + kWsActOffset;
     ActPrepArgs pa = {};
     pa.mode = pro.mode;
@@ -1032,7 +1029,7 @@ cpq_status cpq_argmax(const float *x, int64_t n, int64_t m, int32_t *out, void *
     size_t bytes;
     cpq_status rc = workspace_of_current(&ws, &bytes);
     if (rc) return rc;
-    // aux area after the row-block counters and partials: [rows][chunks] values, indices, then row counters
+    // aux area (after the counters, partials and piece words): [rows][chunks] values, indices, then row counters
     uint8_t *aux = static_cast<uint8_t *>(ws) + kWsAuxOffset;
     float *pval = reinterpret_cast<float *>(aux);
     int32_t *pidx = reinterpret_cast<int32_t *>(aux + size_t(kArgmaxMaxRows) * kArgmaxChunks * 4);
