@@ -29,6 +29,7 @@ EXPORTED = [
     "cpq_mul_mat_multi", "cpq_mul_mat_fused", "cpq_mul_mat_noalloc", "cpq_quantize_act", "cpq_rms_norm",
     "cpq_swiglu", "cpq_add_inplace", "cpq_argmax",
     "cpq_decode_plan_create", "cpq_decode_plan_run", "cpq_decode_plan_destroy",
+    "cpq_trunk_create", "cpq_trunk_run", "cpq_trunk_phases", "cpq_trunk_destroy",
     "cpq_tp_split_state", "cpq_tp_unique_id", "cpq_tp_comm_init", "cpq_tp_allreduce_f32", "cpq_tp_comm_check",
     "cpq_tp_comm_destroy", "cpq_tp_ar_create", "cpq_tp_ar_connect", "cpq_tp_ar_destroy", "cpq_tp_ar_add", "cpq_tp_ar_zero", "cpq_mul_mat_fused_ar",
     "cpq_synth_weights", "cpq_device_status", "cpq_last_error", "cpq_status_string",
@@ -58,6 +59,11 @@ class CpqPrologue(C.Structure):
 class CpqDecodePhase(C.Structure):
     _fields_ = [("mode", C.c_int32), ("n_w", C.c_int32), ("x", C.c_void_p), ("r", C.c_void_p), ("g", C.c_void_p),
                 ("h_out", C.c_void_p), ("eps", C.c_float), ("w", C.POINTER(CpqTensor) * 3), ("y", C.c_void_p * 3)]
+
+
+class CpqTrunkLayer(C.Structure):
+    _fields_ = [(n, C.POINTER(CpqTensor)) for n in ("q", "k", "v", "o", "gate", "up", "down")] + [
+        ("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p), ("o_ranks", C.c_uint32)]
 
 
 PRO_NONE, PRO_RMS, PRO_SWIGLU = 0, 1, 2
@@ -99,6 +105,10 @@ def lib() -> C.CDLL:
         "cpq_decode_plan_create": (st, [P(CpqDecodePhase), C.c_int, C.c_int, P(vp)]),
         "cpq_decode_plan_run": (st, [vp, vp]),
         "cpq_decode_plan_destroy": (None, [vp]),
+        "cpq_trunk_create": (st, [P(CpqTrunkLayer), C.c_int, i64, C.c_float, vp, C.c_int, P(vp)]),
+        "cpq_trunk_run": (st, [vp, vp, vp, vp]),
+        "cpq_trunk_phases": (C.c_int, [vp]),
+        "cpq_trunk_destroy": (None, [vp]),
         "cpq_tp_split_state": (CpqSplitState, [C.c_char_p, P(CpqHparams), i64, i64, C.c_int]),
         "cpq_tp_unique_id": (st, [vp]),
         "cpq_tp_comm_init": (st, [P(vp), C.c_int, C.c_int, vp, C.c_int, C.c_int]),

@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(256, 1) __maxnreg__(AR ? CPQ_ACT_AR_MAXNREG : 
         // r = the sum over ranks of the all-reduced output (LL words, waited for one by one)
         if (threadIdx.x == 0) ar_seq = ar_consumer_begin(a.ar, ticket);
         __syncthreads();
-        const int par = int(ar_seq & 1u);
+        const int par = int(ar_seq % kArSlots);
         rows.n = a.ar.world;
         rows.seq = ar_seq;
         rows.p0 = a.ar.base + int64_t(par) * a.ar.world * a.ar.n_max + int64_t(t) * a.ar.n;

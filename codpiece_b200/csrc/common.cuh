@@ -176,16 +176,20 @@ __device__ __forceinline__ float warp_sum(float v) {
 // (seq << 32 | fp32 bits), written with a single 64-bit store, so a reader
 // that sees the expected sequence number in a word also sees that word's
 // value: no fences, no flags, no counters on the producer side. Every rank's
-// receive buffer holds [2 parities][world][n_max] such words; sequence
-// number s uses parity s & 1.
+// receive buffer holds [kArSlots][world][n_max] such words; sequence number s
+// uses slot s % kArSlots. Two slots would do when every rank contributes to
+// every all-reduce (a rank cannot produce s + 2 before every rank has
+// consumed s); the persistent trunk (trunk.cuh) lets ranks without rows of a
+// projection skip its all-reduce, and four slots keep that safe too.
 
 constexpr int kArMaxRanks = 8;
+constexpr unsigned kArSlots = 4;
 
 // Producer side (row GEMV of a row-parallel projection).
 struct ArOut {
     uint64_t *peer[kArMaxRanks];  // each rank's receive buffer (this rank's included)
     const unsigned *seq;          // this rank's count of consumed all-reduces (local)
-    int64_t n_max;                // words per (parity, rank) slot
+    int64_t n_max;                // words per (slot, rank)
     int64_t n;                    // output rows (token stride in a slot)
     int world, rank;
     int on;

@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(256, 1) ar_add_kernel(const ArIn ar, const flo
     const int t = blockIdx.y;
     const int64_t e0 = (int64_t(blockIdx.x) * 256 + threadIdx.x) * 8;
     if (e0 >= k) return;
-    const uint64_t *base = ar.base + int64_t(seq & 1u) * ar.world * ar.n_max + int64_t(t) * ar.n + e0;
+    const uint64_t *base = ar.base + int64_t(seq % kArSlots) * ar.world * ar.n_max + int64_t(t) * ar.n + e0;
     float v[8];
     ar_sum8(base, ar.n_max, ar.world, seq, v);
     const float4 x0 = *reinterpret_cast<const float4 *>(x + int64_t(t) * k + e0);
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(256) ar_zero_kernel(const ArOut ar, int64_t to
     pdl_wait();
     pdl_launch_dependents();
     const unsigned e = *ar.seq + 1u;
-    const int64_t slot = (int64_t(e & 1u) * ar.world + ar.rank) * ar.n_max;
+    const int64_t slot = (int64_t(e % kArSlots) * ar.world + ar.rank) * ar.n_max;
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x)
         for (int d = 0; d < ar.world; d++) st_relaxed_sys_u64(ar.peer[d] + slot + i, uint64_t(e) << 32);
 }

@@ -133,7 +133,7 @@ struct RowSeg {
 
 // The finished values of one 32-row block (lane = row): stored in Y, or,
 // for an all-reduced output (ar non-null, sequence number ar_e), written to
-// slot (ar_e & 1, rank) of every rank's receive buffer over NVLink as LL
+// slot (ar_e % kArSlots, rank) of every rank's receive buffer over NVLink as LL
 // words (ar_e << 32 | value), one 64-bit store each: nothing else to publish.
 template <int MT>
 __device__ __forceinline__ void row_block_out(const float (&v)[MT], float *y, int64_t y_stride, int m, bool row_ok,
@@ -144,7 +144,7 @@ __device__ __forceinline__ void row_block_out(const float (&v)[MT], float *y, in
             if (t < m && row_ok) y[size_t(t) * y_stride + row] = v[t];
         return;
     }
-    const int64_t slot = (int64_t(ar_e & 1u) * ar->world + ar->rank) * ar->n_max;
+    const int64_t slot = (int64_t(ar_e % kArSlots) * ar->world + ar->rank) * ar->n_max;
     for (int d = 0; d < ar->world; d++) {
         uint64_t *dst = ar->peer[d] + slot;
 #pragma unroll

@@ -11,6 +11,7 @@
 //   gemv_row.cuh     Q4_K decode GEMV (M 1..3), lane per row
 //   gemm_tc.cuh      Q4_K chunked-prefill GEMM (M > 16) on tcgen05 tensor cores
 //   decode.cuh       persistent decode step: a chain of Q4_K GEMV phases in one launch
+//   trunk.cuh        persistent decode trunk: every layer of a rank's step in one launch
 //   elementwise.cuh  rms norm, SwiGLU, residual add, argmax
 //   synth.cuh        seeded synthetic weights
 //   split.inl        tensor-parallel partition rules (host)
@@ -19,6 +20,7 @@
 //   noalloc.inl      cpq_mul_mat_noalloc: decode GEMV on static device scratch
 //   plan.inl         cpq_decode_plan_*: host side of the persistent decode kernel
 //   tp_ar.inl        cpq_tp_ar_*: the fused allreduce channel over NVLink peer memory
+//   trunk.inl        cpq_trunk_*: host side of the persistent decode trunk
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ < 1000
 #error "libcpq targets sm_100a (B200) only"
 #endif
@@ -38,6 +40,7 @@
 #include "gemv_row.cuh"
 #include "gemm_tc.cuh"
 #include "decode.cuh"
+#include "trunk.cuh"
 #include "quantize.cuh"
 #include "synth.cuh"
 #include "split.inl"
@@ -46,3 +49,4 @@
 #include "noalloc.inl"
 #include "plan.inl"
 #include "tp_ar.inl"
+#include "trunk.inl"

@@ -15,35 +15,32 @@ namespace cpq {
 
 // Lane l holds elements 8l..8l+7 of the block in v; on return q holds their
 // quants and the function returns d (the same value in every lane).
+//
+// The element of largest magnitude, first index on ties (the pick of the
+// sequential scan), in two warp reductions: the largest |x| as fp32 bits
+// (monotone for non-negative values), then the smallest index among the
+// lanes that hold it; that lane's signed value comes back by one shuffle.
 __device__ __forceinline__ float q8k_quantize_block(const float (&v)[8], int lane, int (&q)[8]) {
     float amax = 0.0f, mx = 0.0f;
-    int idx = 0x7fffffff;
+    unsigned idx = 0xffffffffu;
 #pragma unroll
     for (int e = 0; e < 8; e++) {
         const float ax = fabsf(v[e]);
         if (ax > amax) {
             amax = ax;
             mx = v[e];
-            idx = lane * 8 + e;
+            idx = unsigned(lane * 8 + e);
         }
     }
-    // largest magnitude, first index on ties: the same pick as the sequential scan
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
-        const float om = __shfl_xor_sync(0xffffffffu, mx, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (oa > amax || (oa == amax && oi < idx)) {
-            amax = oa;
-            mx = om;
-            idx = oi;
-        }
-    }
-    if (amax == 0.0f) {
+    const unsigned abits = __float_as_uint(amax);
+    const unsigned m = __reduce_max_sync(0xffffffffu, abits);
+    if (m == 0u) {
 #pragma unroll
         for (int e = 0; e < 8; e++) q[e] = 0;
         return 0.0f;
     }
+    const unsigned first = __reduce_min_sync(0xffffffffu, abits == m ? idx : 0xffffffffu);
+    mx = __shfl_sync(0xffffffffu, mx, int(first >> 3));
     const float iscale = __fdiv_rn(-127.0f, mx);
 #pragma unroll
     for (int e = 0; e < 8; e++) {

@@ -1,6 +1,6 @@
 // tp_ar.inl — cpq_tp_ar_*: the fused allreduce channel over NVLink peer memory.
 //
-// Each rank allocates one receive buffer of LL words, [2 parities][world]
+// Each rank allocates one receive buffer of LL words, [kArSlots][world]
 // [n_max] u64 (common.cuh), exports it with a CUDA IPC handle and maps the
 // other ranks' buffers (cudaIpcOpenMemHandle, peer access enabled lazily).
 // Its sequence number and the consumers' arrival counter live in a separate,
@@ -94,7 +94,7 @@ extern "C" cpq_status cpq_tp_ar_create(int device, int world, int rank, int64_t 
     ar->world = world;
     ar->rank = rank;
     ar->n_max = int64_t(align_up(size_t(n_max), 64));
-    const size_t bytes = size_t(2) * world * size_t(ar->n_max) * sizeof(uint64_t);
+    const size_t bytes = size_t(kArSlots) * world * size_t(ar->n_max) * sizeof(uint64_t);
     auto done = [&](cpq_status s) {
         if (cur >= 0) cudaSetDevice(cur);
         if (s != CPQ_SUCCESS) ar_free(ar);

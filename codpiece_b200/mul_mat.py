@@ -18,7 +18,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import PRO_NONE, PRO_RMS, PRO_SWIGLU, CpqPrologue, CpqTensor, check, lib
+from ._lib import PRO_NONE, PRO_RMS, PRO_SWIGLU, CpqPrologue, CpqTensor, CpqTrunkLayer, check, lib
 
 TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_K = (
     _lib.TYPE_F32, _lib.TYPE_Q8_0, _lib.TYPE_Q4_K, _lib.TYPE_Q6_K, _lib.TYPE_Q8_K)
@@ -300,6 +300,73 @@ class DecodePlan:
     def close(self) -> None:
         if self.handle:
             lib().cpq_decode_plan_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+@dataclass
+class TrunkLayer:
+    """One layer of a decode trunk (include/cpq.h cpq_trunk_layer): this rank's
+    Q4_K shards; q and o are None on a rank without attention rows in the
+    layer (tensor parallel), o_ranks the bit mask of ranks that hold them
+    (0 = all)."""
+
+    q: QTensor | None
+    k: QTensor | None
+    v: QTensor | None
+    o: QTensor | None
+    gate: QTensor
+    up: QTensor
+    down: QTensor
+    attn_norm: torch.Tensor | None = None
+    ffn_norm: torch.Tensor | None = None
+    o_ranks: int = 0
+
+
+class Trunk:
+    """A rank's whole decode trunk as one persistent kernel (cpq_trunk_*).
+
+    run(h_in, h_out) is one decode step (M = 1): h_out receives the residual
+    stream after the last layer. Pointers are baked in at creation: keep the
+    weights alive (this object holds references). Capturable in a CUDA graph."""
+
+    def __init__(self, layers: list[TrunkLayer], n_embd: int, eps: float = 1e-6, ar: "ArChannel | None" = None,
+                 device: int | None = None):
+        dev = torch.cuda.current_device() if device is None else device
+        self._keep = layers
+        self._descs = []
+        arr = (CpqTrunkLayer * len(layers))()
+        for i, L in enumerate(layers):
+            c = arr[i]
+            for name in ("q", "k", "v", "o", "gate", "up", "down"):
+                w = getattr(L, name)
+                if w is not None:
+                    d = w.desc()
+                    self._descs.append(d)
+                    setattr(c, name, C.pointer(d))
+            c.attn_norm = _ptr(L.attn_norm)
+            c.ffn_norm = _ptr(L.ffn_norm)
+            c.o_ranks = int(L.o_ranks)
+        self._arr = arr
+        self.ar = ar
+        self.handle = C.c_void_p()
+        check(lib().cpq_trunk_create(arr, len(layers), int(n_embd), float(eps), ar.handle if ar is not None else None,
+                                     dev, C.byref(self.handle)), "cpq_trunk_create")
+        self.n_phases = int(lib().cpq_trunk_phases(self.handle))
+
+    def run(self, h_in: torch.Tensor, h_out: torch.Tensor, stream=None) -> torch.Tensor:
+        check(lib().cpq_trunk_run(self.handle, C.c_void_p(h_in.data_ptr()), C.c_void_p(h_out.data_ptr()),
+                                  _stream(stream)), "cpq_trunk_run")
+        return h_out
+
+    def close(self) -> None:
+        if self.handle:
+            lib().cpq_trunk_destroy(self.handle)
             self.handle = C.c_void_p()
 
     def __del__(self):

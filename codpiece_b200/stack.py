@@ -84,7 +84,7 @@ class Stack:
 
     def __init__(self, hp: tp.Hparams, n_layer: int, rank: int = 0, world: int = 1, comm: Comm | None = None,
                  m: int = 1, seed: int = 0, head: bool = True, device: int | None = None, eps: float = 1e-6,
-                 use_plan: bool = False, ar_exchange=None):
+                 use_plan: bool = False, ar_exchange=None, use_trunk: bool = False):
         self.hp, self.n_layer, self.rank, self.world, self.comm, self.m = hp, n_layer, rank, world, comm, m
         self.eps = eps
         self.dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
@@ -130,6 +130,7 @@ class Stack:
         mm.init(self.dev.index, 64 << 20)
         self.graph: torch.cuda.CUDAGraph | None = None
         self.plan: mm.DecodePlan | None = None
+        self.trunk: mm.Trunk | None = None
         # Row-parallel partial sums: through the fused NVLink allreduce when the
         # caller supplies a handle exchange (decode M <= 3 with the head), else NCCL.
         self.ar: mm.ArChannel | None = None
@@ -140,6 +141,12 @@ class Stack:
             if world != 1 or m != 1:
                 raise ValueError("decode plans run the single-GPU M = 1 step")
             self._build_plan()
+        if use_trunk:
+            if m != 1:
+                raise ValueError("the decode trunk runs M = 1 steps")
+            if world > 1 and self.ar is None:
+                raise ValueError("a tensor-parallel trunk needs the fused all-reduce channel (ar_exchange)")
+            self._build_trunk()
 
     # -- bytes -------------------------------------------------------------
     def weight_bytes(self) -> int:
@@ -160,6 +167,8 @@ class Stack:
             return (1 if prologue else 0) + 2 * groups
 
         n = 0
+        if self.trunk is not None:
+            return 1 + (fused(mm.TYPE_Q6_K, True) + 1 if self.head is not None else 0)
         if self.plan is not None:
             return 1 + fused(mm.TYPE_Q6_K, True) + 1 if self.head is not None else 1
         for il, lw in enumerate(self.layers):
@@ -174,6 +183,20 @@ class Stack:
         else:
             n += 1
         return n
+
+    def _build_trunk(self) -> None:
+        """The whole trunk of step_body() as one persistent kernel (cpq_trunk_*);
+        the head stays a fused call + argmax. o_ranks: the ranks with attention
+        rows in each layer (at TP8 the split rules give them to half of the ranks)."""
+        layers = []
+        for sh, lw in zip(self.shards, self.layers):
+            o_ranks = 0
+            for r, (q0, q1) in enumerate(sh.q):
+                if q1 > q0:
+                    o_ranks |= 1 << r
+            layers.append(mm.TrunkLayer(q=lw.q, k=lw.k, v=lw.v, o=lw.o, gate=lw.gate, up=lw.up, down=lw.down,
+                                        o_ranks=o_ranks if self.world > 1 else 0))
+        self.trunk = mm.Trunk(layers, self.hp.n_embd, eps=self.eps, ar=self.ar, device=self.dev.index)
 
     def _build_plan(self) -> None:
         """The 64-layer trunk of step_body() as one decode plan (4 phases per
@@ -216,6 +239,13 @@ class Stack:
         On return self.h holds the final residual stream."""
         h, h_alt = self.h, self.h_alt
         part_live = False  # self.part holds a projection output still to be added to h
+        if self.trunk is not None:
+            self.trunk.run(h, h_alt)
+            if self.head is not None:
+                mm.mul_mat_fused([self.head], h_alt, [self.logits], mode=mm.PRO_RMS, eps=self.eps)
+                mm.argmax(self.logits, out=self.tok)
+            self.h_final = h_alt
+            return
         if self.plan is not None:
             self.plan.run()
             h, h_alt = self._plan_h
@@ -307,6 +337,9 @@ class Stack:
 
     def release(self) -> None:
         self.graph = None
+        if self.trunk is not None:
+            self.trunk.close()
+            self.trunk = None
         if self.ar is not None:
             self.ar.close()
             self.ar = None

@@ -274,14 +274,16 @@ cpq_status cpq_tp_comm_destroy(cpq_comm *comm, int abort);
  * Protocol (LL, as in NCCL's LL): each value travels with the all-reduce's
  * sequence number s in one 64-bit word written by a single store, so a
  * reader that sees s in a word also sees its value; nothing else is
- * published. All ranks run the same sequence of all-reduces; s alternates
- * between two buffer halves (s & 1), and a rank cannot produce s + 2 before
- * every rank has consumed s. A consumer waits for each word at most 2 s
- * (then the device error word is set).
+ * published. All ranks run the same sequence of all-reduces; s selects one
+ * of four buffer slots (s % 4). A rank cannot produce s + 2 before every
+ * rank that contributes to s + 1 has consumed s, so four slots also stay
+ * safe when some ranks contribute nothing to an all-reduce (the persistent
+ * trunk below). A consumer waits for each word at most 2 s (then the device
+ * error word is set).
  */
 typedef struct cpq_tp_ar cpq_tp_ar;
 
-/* Allocates this rank's receive buffer (n_max floats per rank and parity,
+/* Allocates this rank's receive buffer (n_max floats per rank and slot,
  * n_max >= M * N of the projections) on `device` and writes its CUDA IPC
  * handle (64 bytes) to handle64. world <= 8. */
 cpq_status cpq_tp_ar_create(int device, int world, int rank, int64_t n_max, cpq_tp_ar **ar, void *handle64);
@@ -312,6 +314,54 @@ cpq_status cpq_tp_ar_zero(cpq_tp_ar *ar, int64_t n, int64_t m, void *stream);
  * CPQ_ERR_UNSUPPORTED. */
 cpq_status cpq_mul_mat_fused_ar(const cpq_tensor *const *w, cpq_tensor *const *y, int n_w, const cpq_tensor *x,
                                 const cpq_prologue *pro, cpq_tp_ar *r_ar, cpq_tp_ar *y_ar, void *stream);
+
+/* ---- the decode trunk: every layer of a decode step in one launch -----------
+ *
+ * The batch-1 decode trunk of one rank (codpiece's qwen35 layer,
+ * qwen35.rs:2554-2786: rms -> q/k/v, o, rms -> gate/up, swiglu -> down, with
+ * the residual adds) as one persistent kernel: every projection's weights
+ * stream through TMA rings that run ahead across projection boundaries, the
+ * hand-offs between projections are flagged words instead of kernel
+ * boundaries, and under tensor parallelism the row-parallel partial sums
+ * (o, down) cross NVLink inside the same kernel (the channel of
+ * cpq_tp_ar_*). No reference counterpart: it fuses the consecutive
+ * ggml_mul_mat nodes of a decode graph, each with the semantics of one
+ * cpq_mul_mat_fused call at M = 1 (Q8_K re-quantization, integer block dots).
+ * The attention core is not part of it: q stands in for the attention output
+ * that feeds o (the benchmark's attention-free stack). */
+typedef struct cpq_trunk_layer {
+    const cpq_tensor *q, *k, *v; /* Q4_K [n_embd -> this rank's rows]; q (and o) NULL: no attention rows
+                                    on this rank in this layer (tensor parallel only); k, v may be NULL */
+    const cpq_tensor *o;         /* Q4_K [q rows -> n_embd]: this rank's K slice (row-parallel) */
+    const cpq_tensor *gate, *up; /* Q4_K [n_embd -> this rank's ffn rows] */
+    const cpq_tensor *down;      /* Q4_K [ffn rows -> n_embd]: this rank's K slice (row-parallel) */
+    const float *attn_norm;      /* RMS weight [n_embd] before q/k/v, or NULL */
+    const float *ffn_norm;       /* RMS weight [n_embd] before gate/up, or NULL */
+    uint32_t o_ranks;            /* ranks holding attention rows in this layer (bit mask); 0 = all */
+} cpq_trunk_layer;
+
+typedef struct cpq_trunk cpq_trunk;
+
+/* Validates the layers and builds the device-side phase table for `device`
+ * (allocates device memory: call outside stream capture). ar is NULL on a
+ * single GPU, else this rank's connected channel (n_max >= n_embd); every
+ * rank of the group must create its trunk with the same layer count and
+ * o_ranks. n_embd is a multiple of 256 up to 6144; q and ffn row counts are
+ * multiples of 256. The weight pointers are baked in. */
+cpq_status cpq_trunk_create(const cpq_trunk_layer *layers, int n_layers, int64_t n_embd, float eps, cpq_tp_ar *ar,
+                            int device, cpq_trunk **trunk);
+/* One decode step: h_out = the residual stream after the last layer for the
+ * input h_in (n_embd floats each, device pointers, distinct). Capturable; one
+ * cooperative launch of one CTA per SM. Runs of one trunk must not overlap
+ * on the GPU; under tensor parallelism every rank runs its trunk once per
+ * step. A bounded wait that gives up sets the device error word
+ * (cpq_device_status). */
+cpq_status cpq_trunk_run(cpq_trunk *trunk, const float *h_in, float *h_out, void *stream);
+/* Phases in the trunk's table (4 per layer, plus a final fold under tensor
+ * parallelism). */
+int cpq_trunk_phases(const cpq_trunk *trunk);
+/* Frees the trunk (after its last run has completed). NULL is ignored. */
+void cpq_trunk_destroy(cpq_trunk *trunk);
 
 /* ---- synthetic weights ----------------------------------------------------- */
 

@@ -129,3 +129,28 @@ def test_plan_and_channel_arguments_are_validated_on_the_host(L):
     assert L.cpq_tp_ar_connect(None, h) == 1
     assert L.cpq_tp_ar_add(None, None, None, 8, 1, None) == 1
     L.cpq_tp_ar_destroy(None)
+
+
+def test_trunk_arguments_are_validated_on_the_host(L):
+    """cpq_trunk_create rejects bad arguments before any device call."""
+    from codpiece_b200 import _lib
+    t = C.c_void_p()
+    layers = (_lib.CpqTrunkLayer * 1)()
+    assert L.cpq_trunk_create(None, 1, 5120, 1e-6, None, 0, C.byref(t)) == 1     # no layers
+    assert L.cpq_trunk_create(layers, 0, 5120, 1e-6, None, 0, C.byref(t)) == 1
+    assert L.cpq_trunk_create(layers, 1, 5120, 1e-6, None, 0, None) == 1
+    assert L.cpq_trunk_create(layers, 1, 5000, 1e-6, None, 0, C.byref(t)) == 2   # n_embd not a multiple of 256
+    assert L.cpq_trunk_create(layers, 1, 256 * 25, 1e-6, None, 0, C.byref(t)) == 2  # above the RMS image limit
+    q = _lib.CpqTensor()
+    q.type = 12
+    q.ne[:] = [5120, 256, 1, 1]
+    q.nb[:] = [144, 2880, 2880 * 256, 2880 * 256]
+    q.data = 0x1000
+    layers[0].q = C.pointer(q)                                                   # q without o
+    assert L.cpq_trunk_create(layers, 1, 5120, 1e-6, None, 0, C.byref(t)) == 1
+    assert b"q and o" in L.cpq_last_error()
+    layers[0].q = None                                                           # no attention on one rank
+    assert L.cpq_trunk_create(layers, 1, 5120, 1e-6, None, 0, C.byref(t)) == 1
+    assert not t.value
+    L.cpq_trunk_destroy(None)                                                    # NULL is ignored
+    assert L.cpq_trunk_run(None, None, None, None) == 1
