@@ -7,9 +7,13 @@
 // cudaMalloc/cudaFree can cause. For them
 // this entry point runs the decode GEMV (gemv_row.cuh, unchanged) with every
 // byte of its scratch — the quantized activation image and the tail-cut
-// words the CTAs hand each other — in one file-scope device array that is
-// reserved when the library is loaded and held by every GPU that loads it
-// until the process exits.
+// words the CTAs hand each other — in one file-scope device array that every
+// GPU using the library holds until the process exits. CUDA loads a module
+// lazily by default, so the array is set up on a device by the library's
+// first use there (this entry point's first call, or any other cpq call
+// that launches a kernel); that first use may itself allocate and
+// synchronize, so make it at start-up, before any stream capture and away
+// from latency-critical threads.
 //
 // In host code the array's name stands for a host-side shadow, not a device
 // address, so its device address is looked up once per device with
@@ -66,8 +70,12 @@ static cudaError_t noalloc_launch_row(RowArgs &a, int smem, cudaStream_t st) {
     auto kern = gemv_q4k_row_kernel<MT>;
     const int dev = current_device();
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
-    if (e != cudaSuccess) return e;
+    static std::atomic<int> set[kMaxDevices];  // the shared-memory attribute, once per device and instance
+    if (!set[dev].load(std::memory_order_relaxed)) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        if (e != cudaSuccess) return e;
+        set[dev].store(1, std::memory_order_relaxed);
+    }
     const int64_t grid = row_grid(a, std::min<int64_t>(sm_count(dev), kNoAllocMaxCtas));
     return launch(kern, dim3(unsigned(grid)), dim3(kRowWarps * 32), size_t(smem), st, a);
 }

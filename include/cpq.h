@@ -134,13 +134,16 @@ cpq_status cpq_mul_mat_fused(const cpq_tensor *const *w, cpq_tensor *const *y, i
  * owns every device allocation, or on a thread that must not take the
  * implicit device synchronization of cudaMalloc/cudaFree). Same result as
  * cpq_mul_mat, but all scratch lives in one static device array of about
- * 1.3 MB that the library reserves on every
- * GPU that loads it, held until the process exits; no cudaMalloc, no
- * cudaFree, no cpq_init needed. Limits: Q4_K weights only, M <= 3 tokens,
- * K <= 32768, N <= 262144 rows; anything larger returns CPQ_ERR_UNSUPPORTED
- * without launching. The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress), so make it before any stream capture. All
- * calls share the array: calls whose executions overlap on the GPU race. */
+ * 1.3 MB that every GPU using the library holds until the process exits;
+ * no cudaMalloc, no cudaFree, no cpq_init needed. Limits: Q4_K weights only,
+ * M <= 3 tokens, K <= 32768, N <= 262144 rows; anything larger returns
+ * CPQ_ERR_UNSUPPORTED without launching. CUDA sets up the library's module
+ * (and so the array) on a device at the library's first use there, and the
+ * first call of this entry point on a device also looks up the array's
+ * device address (cudaGetSymbolAddress): both may allocate or synchronize,
+ * so make the first call at start-up, before any stream capture and away from
+ * latency-critical threads. All calls share the array: calls whose
+ * executions overlap on the GPU race. */
 cpq_status cpq_mul_mat_noalloc(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *y, void *stream);
 
 /* Activation re-quantization as ggml-cpu's from_float for the vec_dot_type of

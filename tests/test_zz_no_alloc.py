@@ -4,7 +4,7 @@ Callers that run the product inside a host engine that owns all device
 memory, or on a thread that must not take cudaMalloc's implicit device
 synchronization, call cpq_mul_mat_noalloc: the same
 Q4_K decode product as cpq_mul_mat, with its scratch in a static device array
-the library reserves at load time instead of a workspace. These checks call
+every GPU using the library holds until exit, instead of a workspace. These checks call
 it through the C ABI, twice in a row (the array keeps the previous call's
 contents), and compare each result with cpq_mul_mat's within the parity
 tolerance; sizes beyond the array's limits must be refused without a launch.
@@ -22,7 +22,7 @@ from tests.conftest import TOL, rel_err
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("n,k,m", [(17408, 5120, 1), (5120, 17408, 1), (1031, 2048, 3)])
+@pytest.mark.parametrize("n,k,m", [(17408, 5120, 1), (5120, 17408, 1), (17408, 5120, 2), (1031, 2048, 3)])
 def test_noalloc_matches_cpq_mul_mat_on_two_calls_in_a_row(cuda, n, k, m):
     from codpiece_b200 import _lib
     from codpiece_b200 import mul_mat as mm
