@@ -4,13 +4,21 @@
 Workload (every N): the 27B-shaped stack of BASELINE config 5 --
 64 layers of Q4_K q/k/v/o/gate/up/down (hidden 5120, q 6144, kv 1024,
 FFN 17408) plus a mirrored Q6_K head over vocab 151936 -- decoding M = 1
-token per step, tensor-parallel over N GPUs (one process per GPU; the
-row-parallel partial sums are all-reduced through the fused NVLink channel,
-or through NCCL with --nccl). Its FFN projections are
-exactly BASELINE config 2's Q4_K mat-vec shapes, 64 times over.
+token per step, tensor-parallel over N GPUs (one process per GPU). Each
+rank's 64 layers run as one persistent trunk kernel (cpq_trunk_run) whose
+row-parallel partial sums cross NVLink inside the kernel; the head is a
+fused Q6_K mul_mat plus argmax. --per-call runs the trunk as one fused call
+per projection instead, --nccl (with --per-call) all-reduces through NCCL.
+Its FFN projections are exactly BASELINE config 2's Q4_K mat-vec shapes,
+64 times over.
 
-  value      aggregate weight GB/s = weight bytes all ranks stream per step /
-             max-over-ranks step time (CUDA events, inputs resident in HBM)
+  value      model GB/s = the unsharded model's weight bytes (12.906 GB, the
+             head counted once) / max-over-ranks ms per token (CUDA events,
+             inputs resident in HBM); bytes each rank streams (the mirrored
+             head on every rank) are config.weight_bytes_per_rank
+  tp_parity  N > 1: a 2-layer stack decoded (M = 1, trunk) and verified
+             (M = 8, NCCL) on all ranks against the same stack on one GPU
+             before timing; the run fails if either differs by more than 1e-3
   e2e        the same through the public API with host buffers: hidden state
              uploaded from pinned memory and the greedy token read back
              every step
@@ -25,7 +33,7 @@ exactly BASELINE config 2's Q4_K mat-vec shapes, 64 times over.
              mul_mat (activation pre-pass included) against
              MEASURED_PEAKS.json bf16_tflops
   verify     the same 64-layer stack stepping M = 8 tokens (the speculative
-             verify batch of configs[4]), 1 GPU
+             verify batch of configs[4]) on all N GPUs (NCCL all-reduce)
   small_configs  configs[0] (Q8_0 [5120 x 5120] mat-vec, M = 1) and configs[2]
              (one layer's q/k/v/o and the Q6_K head at M = 2, 4, 8, 16):
              weight GB/s of each mul_mat on rotating weights larger than L2
@@ -38,7 +46,8 @@ same stack (a few layers per step) and prints the same metric.
 inside an NVTX range named "step" (ncu --nvtx --nvtx-include step/):
   decode_ffn   Q4_K mul_mat M=1 on config 2's gate and down shapes, 2 calls each
   prefill_512  Q4_K mul_mat M=512 on [17408 x 5120], 1 call
-  stack        --steps replays of the captured stack decode step
+  stack        --steps replays of the captured stack decode step (the trunk kernel at M = 1
+               unless --per-call)
   head         Q6_K mul_mat on the head [151936 x 5120] at M = 1 and M = 8, 1 call each
 """
 from __future__ import annotations
@@ -315,14 +324,24 @@ def small_configs(torch, mm):
     return out
 
 
-def verify_step(torch, st, tp, layers: int, m: int = 8, steps: int = 10):
-    """configs[4]'s verify step: the same stack at M = 8 tokens (MMA GEMVs, NCCL-free at TP1)."""
-    stack = st.Stack(tp.HP_BENCH_27B, layers, 0, 1, None, m=m, seed=0)
-    stack.h.copy_(torch.randn(m, 5120, device="cuda"))
+def model_bytes(tp, layers: int, head: bool = True) -> int:
+    """Weight bytes of the unsharded stack: Q4_K 144 B per 256 weights, the Q6_K head 210 B per 256."""
+    hp = tp.HP_BENCH_27B
+    e, q, kv, ff = hp.n_embd, hp.n_head * hp.head_k, hp.n_head_kv * hp.head_k, hp.n_ff
+    per_layer = sum(n * k // 256 * 144 for n, k in ((q, e), (kv, e), (kv, e), (e, q), (ff, e), (ff, e), (e, ff)))
+    return layers * per_layer + (hp.n_vocab * e // 256 * 210 if head else 0)
+
+
+def verify_step(torch, st, tp, layers: int, rank: int, world: int, comm, barrier, m: int = 8, steps: int = 10):
+    """configs[4]'s verify step: the same stack at M = 8 tokens on all ranks (MMA GEMVs; at N > 1 the
+    row-parallel partial sums go through NCCL). Max over ranks of the device time."""
+    stack = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=0)
+    stack.h.copy_(torch.randn(m, 5120, generator=torch.Generator().manual_seed(5)).cuda())
     stack.capture()
     for _ in range(3):
         stack.replay()
     torch.cuda.synchronize()
+    barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
@@ -330,10 +349,47 @@ def verify_step(torch, st, tp, layers: int, m: int = 8, steps: int = 10):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
-    wb = stack.weight_bytes()
     stack.release()
-    return {"m": m, "ms_per_step": round(ms, 4), "tok_per_s": round(m * 1e3 / ms, 1),
-            "weight_GBs": round(wb / ms / 1e6, 1), "layers": layers}
+    return ms
+
+
+def tp_parity(torch, st, tp, comm, exchange, rank: int, world: int, layers: int = 2):
+    """N > 1: a few full-width layers decoded through the trunk (M = 1, fused NVLink all-reduce) and
+    verified (M = 8, NCCL) on all ranks, against the same stack on rank 0's GPU alone (the per-call path,
+    itself checked against the CPU oracle by the tests). Returns rank 0's verdict."""
+    import torch.distributed as dist
+    out = {}
+    for m, trunk in ((1, True), (8, False)):
+        h0 = torch.randn(m, 5120, generator=torch.Generator().manual_seed(11 + m)) * 2
+        s = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=5,
+                     ar_exchange=exchange if trunk else None, use_trunk=trunk)
+        s.h.copy_(h0)
+        s.step_body()
+        torch.cuda.synchronize()
+        h_tp, logits_tp, tok_tp = s.h_final.cpu(), s.logits.cpu(), s.tok.cpu()
+        toks = [None] * world
+        dist.all_gather_object(toks, tok_tp.tolist())
+        s.release()
+        del s
+        if rank == 0:
+            ref = st.Stack(tp.HP_BENCH_27B, layers, 0, 1, None, m=m, seed=5)
+            ref.h.copy_(h0)
+            ref.step_body()
+            torch.cuda.synchronize()
+            lr, hr = ref.logits.cpu(), ref.h_final.cpu()
+            key = "decode_m1_trunk" if trunk else "verify_m8_nccl"
+            out[key] = {"h_rel": float((h_tp - hr).abs().max() / hr.abs().max()),
+                        "logits_rel": float((logits_tp - lr).abs().max() / lr.abs().max()),
+                        "tok_match": tok_tp.tolist() == ref.tok.cpu().tolist(),
+                        "ranks_agree": all(t == toks[0] for t in toks)}
+            ref.release()
+            del ref
+        dist.barrier()
+    if rank == 0:
+        out["layers"] = layers
+        out["ok"] = all(v["h_rel"] <= 1e-3 and v["logits_rel"] <= 1e-3 and v["ranks_agree"]
+                        for k, v in out.items() if isinstance(v, dict))
+    return out
 
 
 def profile_case(args) -> int:
@@ -382,7 +438,8 @@ def profile_case(args) -> int:
     elif args.profile == "stack":
         from codpiece_b200 import stack as st
         from codpiece_b200 import tp
-        stack = st.Stack(tp.HP_BENCH_27B, args.layers, 0, 1, None, m=args.m, seed=0)
+        stack = st.Stack(tp.HP_BENCH_27B, args.layers, 0, 1, None, m=args.m, seed=0,
+                         use_trunk=args.m == 1 and not args.per_call)
         stack.h.copy_(torch.randn(args.m, 5120, device="cuda"))
         stack.capture()
         for _ in range(args.warmup):
@@ -463,7 +520,9 @@ def main() -> int:
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-verify", action="store_true")
     ap.add_argument("--no-small", action="store_true", help="skip the configs[0] / configs[2] lines")
-    ap.add_argument("--nccl", action="store_true", help="TP partial sums through NCCL instead of the fused allreduce")
+    ap.add_argument("--nccl", action="store_true", help="with --per-call: TP partial sums through NCCL")
+    ap.add_argument("--per-call", action="store_true", help="one fused call per projection instead of the trunk kernel")
+    ap.add_argument("--no-parity", action="store_true", help="skip the N > 1 parity check")
     ap.add_argument("--profile", default=None, choices=["decode_ffn", "prefill_512", "stack", "head"])
     args = ap.parse_args()
     if args.profile:
@@ -509,9 +568,27 @@ def main() -> int:
         dist.all_gather_object(got, handle)
         return got
 
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    parity = None
+    if world > 1 and not args.no_parity:
+        parity = tp_parity(torch, st, tp, comm, exchange, rank, world)
+        ok = [parity.get("ok", True) if rank == 0 else True]
+        dist.broadcast_object_list(ok, src=0)
+        if not ok[0]:
+            if rank == 0:
+                log(f"TP parity check failed: {parity}")
+            comm.destroy()
+            dist.destroy_process_group()
+            return 3
+        torch.cuda.empty_cache()
+
+    use_trunk = args.m == 1 and not args.per_call
     t_build = time.perf_counter()
     stack = st.Stack(tp.HP_BENCH_27B, args.layers, rank, world, comm, m=args.m, seed=0,
-                     ar_exchange=exchange if (world > 1 and not args.nccl) else None)
+                     ar_exchange=exchange if (world > 1 and not args.nccl) else None, use_trunk=use_trunk)
     g = torch.Generator(device="cpu").manual_seed(1234)
     h0 = torch.randn(args.m, 5120, generator=g).cuda()
     stack.h.copy_(h0)
@@ -519,10 +596,6 @@ def main() -> int:
     torch.cuda.synchronize()
     log(f"[rank {rank}] stack built + captured in {time.perf_counter() - t_build:.1f} s, "
         f"{stack.weight_bytes() / 1e9:.3f} GB of weights on this rank")
-
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local])
 
     cur = torch.cuda.current_stream()
     for _ in range(args.warmup):
@@ -574,9 +647,10 @@ def main() -> int:
     b = torch.tensor([float(stack.weight_bytes())], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(b, op=dist.ReduceOp.SUM)
+        dist.all_reduce(b, op=dist.ReduceOp.MAX)
     ms, ms_e2e = float(t[0]), float(t[1])
-    total_bytes = float(b[0])
+    rank_bytes = float(b[0])
+    total_bytes = float(model_bytes(tp, args.layers))
     launches = stack.launches_per_step() * args.steps
 
     roof = prefill = verify = None
@@ -588,13 +662,23 @@ def main() -> int:
         if world == 1 and not args.no_small:
             small = small_configs(torch, mm)
     barrier()
-    if world == 1 and not args.no_verify:
-        verify = verify_step(torch, st, tp, args.layers)
-    barrier()
-
     ar_mode = ("none" if world == 1 else "nccl" if stack.ar is None else
+               "inside the trunk kernel over NVLink peer memory (cpq_trunk_run)" if stack.trunk is not None else
                "fused into the GEMV over NVLink peer memory (cpq_mul_mat_fused_ar)")
+    path = "trunk" if stack.trunk is not None else "per-call"
     stack.release()
+    del stack
+    torch.cuda.empty_cache()
+    if not args.no_verify:
+        vms = verify_step(torch, st, tp, args.layers, rank, world, comm, barrier)
+        tv = torch.tensor([vms], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(tv, op=dist.ReduceOp.MAX)
+        vms = float(tv[0])
+        verify = {"m": 8, "ms_per_step": round(vms, 4), "tok_per_s": round(8e3 / vms, 1),
+                  "model_GBs": round(total_bytes / vms / 1e6, 1), "layers": args.layers,
+                  "tp_allreduce": "none" if world == 1 else "nccl"}
+    barrier()
     if comm is not None:
         comm.destroy()
     if world > 1:
@@ -613,13 +697,15 @@ def main() -> int:
         "vs_baseline": None, "dtype": "int8 dots (Q4_K/Q6_K x Q8_K), fp32 accumulate", "data": "synthetic",
         "config": {"workload": "27B-shaped stack decode (BASELINE config 5): 64 x Q4_K q/k/v/o/gate/up/down + "
                                "mirrored Q6_K head [151936x5120], M=1, TP=N",
+                   "path": path,
                    "tp_allreduce": ar_mode,
                    "layers": args.layers, "m": args.m, "tp": world, "hidden": 5120, "ffn": 17408,
                    "vocab": 151936, "parallelism": f"tp{world}",
-                   "weight_bytes_all_ranks": int(total_bytes),
+                   "model_bytes": int(total_bytes),
+                   "weight_bytes_per_rank": int(rank_bytes),
                    "ms_per_token": round(ms, 4), "tok_per_s": round(1e3 / ms * args.m, 2),
                    "l2": "weights per rank exceed L2 (126 MB) every step; no flush needed",
-                   "frac_of_hbm_per_gpu": round(value / world / hbm, 4)},
+                   "frac_of_hbm_per_rank": round(rank_bytes / (ms / 1e3) / 1e9 / hbm, 4)},
         "e2e": {"value": round(total_bytes / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(ms_e2e, 4), "h2d_bytes_per_step": 4 * 5120 * args.m,
                 "d2h_bytes_per_step": 4 * args.m},
@@ -629,6 +715,7 @@ def main() -> int:
         "cpu_baseline": cpu,
         "prefill": prefill,
         "verify": verify,
+        "tp_parity": parity,
         "small_configs": small,
     }
     print(json.dumps(line), flush=True)
