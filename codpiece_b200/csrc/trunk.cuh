@@ -9,27 +9,31 @@
 // whole trunk (a table of phases, one per projection group) as one
 // cooperative launch of one CTA per SM:
 //
-//  * Weights. Every warp owns a ring of TMA stages (32 rows x one
-//    superblock, no multicast) whose issue cursor walks the warp's share of
-//    phase p, then of phase p+1, ...: the next projections' weights are in
-//    flight while the current one's input is still being produced.
+//  * Weights. Each of the 8 compute warps owns a ring of TMA stages (32 rows
+//    x one superblock, no multicast). A ninth warp (the first of a third
+//    warpgroup, which hands most of its registers to the compute warps)
+//    issues the copies: its lane w walks compute warp w's share of phase p, then of phase p+1, ...,
+//    and refills a stage as soon as the compute warp has read it (full /
+//    empty mbarriers), so the next projections' weights are in flight while
+//    the current one's input is still being produced, and no compute warp
+//    ever waits for the TMA unit to accept a copy.
 //  * Work split inside a phase: the CTA-range split of the decode GEMV
 //    (gemv_row.cuh), with its in-CTA combination of row-block parts and the
 //    tail-cut hand-off to the next CTA.
 //  * Hand-offs between phases. Every CTA that produced outputs of phase p
 //    adds one to phase p's counter; a CTA that reads them waits (one thread,
 //    short back-off) until the counter holds all of the phase's CTAs, then
-//    copies the values into shared memory with one bulk copy (TMA) per
-//    48 KB. There is no grid barrier: a CTA waits only for the phase it
-//    reads, with its ring of next weights already in flight. The values are
+//    loads the values (all of a lane's loads in flight together; not through
+//    the TMA unit, whose queue is full of weight copies at that moment).
+//    There is no grid barrier: a CTA waits only for the phase it reads, with
+//    its ring of next weights already in flight. The values are
 //    flagged 64-bit words (epoch << 32 | fp32 bits, one store each), so
 //    every value read is checked to be this phase's (and waited for alone
 //    if not): correctness rests on the words, the counter (relaxed, no fence
 //    on the producer side) only says when to start copying. The residual
 //    stream lives in one such vector (R, n_embd words), the q output in QB,
 //    the SwiGLU product in AB; inside every 256-element block the words are
-//    stored in the order tr_swz() gives, so that the lanes' 16-byte reads of
-//    the staged copy hit distinct shared-memory banks.
+//    stored in the order tr_swz() gives (a lane's 16-byte pairs permuted).
 //  * gate/up run as pairs: a stage holds 16 gate rows and the same 16 up
 //    rows, so the warp that finishes them stores silu(gate) * up directly.
 //  * Under tensor parallelism the row-parallel outputs (o, down) go to every
@@ -58,18 +62,24 @@
 
 namespace cpq {
 
-constexpr int kTrWarps = 8;
+constexpr int kTrWarps = 8;                                // compute warps: warpgroups 0 and 1
+constexpr int kTrThreads = (kTrWarps + 4) * 32;           // + warpgroup 2, whose first warp issues the copies
+// Registers: launched at kTrRegLaunch per thread; the copy warpgroup gives
+// back down to kTrRegCopy and the compute warpgroups take kTrRegCompute, so
+// that 128 * kTrRegCopy + 256 * kTrRegCompute == 384 * kTrRegLaunch.
+constexpr int kTrRegLaunch = 168, kTrRegCopy = 56, kTrRegCompute = 224;
+static_assert(128 * kTrRegCopy + 256 * kTrRegCompute <= kTrThreads * kTrRegLaunch, "register split");
+static_assert(kTrThreads * kTrRegLaunch <= 65536, "registers at launch");
 static_assert(kTrWarps == kRowWarps, "the in-CTA combination is sized for kRowWarps");
-constexpr int kTrStages = 4;
+constexpr int kTrStages = 5;
 constexpr int kTrMaxW = 3;
 constexpr int kTrMaxFold = 2;
 constexpr int kTrRmsBlocks = 3;                           // 256-blocks per warp of an RMS image (K <= 24 * 256)
-constexpr int kTrStgBlocks = 24;                          // 256-blocks staged per bulk copy
-constexpr int kTrStgBytes = kTrStgBlocks * kQK_K * 8;     // 48 KB
-constexpr int kTrHdrBytes = 512;                          // stage barriers, staging barrier, RMS partial sums
+constexpr int kTrVecBatch = 2;                            // 256-blocks per warp whose loads are in flight together
+constexpr int kTrBarBytes = kTrWarps * kTrStages * 8;     // one array of stage barriers
+constexpr int kTrHdrBytes = 1024;                         // full and empty stage barriers, RMS partial sums
 constexpr int kTrRingBytes = kTrWarps * kTrStages * kRowStageBytes;
-static_assert(kTrWarps * kTrStages * 8 <= 256, "trunk header: stage barriers");
-static_assert(kTrRmsBlocks * 8 == kTrStgBlocks, "an RMS image is staged in one copy");
+static_assert(2 * kTrBarBytes + 64 <= kTrHdrBytes, "trunk header");
 
 enum : int { kTrInR = 0, kTrInVec = 1 };
 enum : int { kTrOutVec = 0, kTrOutPair = 1, kTrOutResid = 2, kTrOutAr = 3 };
@@ -233,36 +243,40 @@ __device__ __forceinline__ int tr_weight_of(const TrRange &r, int64_t mb) {
     return (r.n_w > 1 && mb >= r.mbs1) + (r.n_w > 2 && mb >= r.mbs2);
 }
 
-// Thread 0 copies blocks [b0, b0 + nb) of a flagged vector into stg with one
-// bulk copy; every thread waits for it (bounded). On a give-up the callers
-// carry on through the same barriers (the error word is set; the next phase
-// start stops the kernel).
-__device__ __forceinline__ bool tr_stage(const uint64_t *src, int b0, int nb, uint8_t *stg, uint64_t *ibar,
-                                         uint32_t &iphase) {
-    if (threadIdx.x == 0) {
-        const uint32_t bytes = uint32_t(nb) * kQK_K * 8;
-        fence_proxy_async_smem();  // the generic reads of the previous staged copy come first
-        mbar_arrive_expect_tx(ibar, bytes);
-        bulk_g2s(stg, src + int64_t(b0) * kQK_K, bytes, ibar);
-    }
-    const bool ok = mbar_wait_bounded(ibar, iphase);
-    iphase ^= 1u;
-    return ok;
+// Barrier 1 among the 256 threads of the compute warps (the copy warp never
+// joins it), plain and with a reduction of a predicate.
+__device__ __forceinline__ void tr_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+__device__ __forceinline__ int tr_bar_or(int pred) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred a, b;\n\tsetp.ne.s32 a, %1, 0;\n\tbar.red.or.pred b, 1, 256, a;\n\tselp.s32 %0, 1, 0, b;\n\t}"
+        : "=r"(r)
+        : "r"(pred)
+        : "memory");
+    return r;
 }
 
-// This lane's 8 values (elements 8l..8l+7) of a staged 256-block: four
-// conflict-free 16-byte reads; a word without epoch ep (the copy raced its
-// writer) is read again from global memory (g_blk), waiting for it.
-__device__ __forceinline__ void tr_read8(const uint64_t *stg_blk, const uint64_t *g_blk, uint32_t ep, float (&v)[8]) {
+__device__ __forceinline__ void ld_relaxed_gpu_v2u64(const uint64_t *p, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// This lane's 8 words (elements 8l..8l+7, in element order) of the 256-block
+// at blk: four 16-byte loads issued back to back (tr_swz order in memory).
+__device__ __forceinline__ void tr_load_lane(const uint64_t *blk, uint64_t (&w)[8]) {
     const int lane = threadIdx.x & 31, k = (lane >> 1) & 3;
 #pragma unroll
-    for (int c = 0; c < 4; c++) {
-        const int pos = 8 * lane + 2 * (c ^ k);
-        const ulonglong2 w = *reinterpret_cast<const ulonglong2 *>(stg_blk + pos);
-        const uint64_t w0 = uint32_t(w.x >> 32) == ep ? w.x : flagged_word_gpu(g_blk + pos, ep);
-        const uint64_t w1 = uint32_t(w.y >> 32) == ep ? w.y : flagged_word_gpu(g_blk + pos + 1, ep);
-        v[2 * c] = __uint_as_float(uint32_t(w0));
-        v[2 * c + 1] = __uint_as_float(uint32_t(w1));
+    for (int c = 0; c < 4; c++) ld_relaxed_gpu_v2u64(blk + 8 * lane + 2 * (c ^ k), w[2 * c], w[2 * c + 1]);
+}
+
+// The values of tr_load_lane's words; a word without epoch ep is waited for
+// on its own (it was loaded before its writer's store arrived).
+__device__ __forceinline__ void tr_check_lane(const uint64_t *blk, uint32_t ep, const uint64_t (&w)[8], float (&v)[8]) {
+    const int lane = threadIdx.x & 31, k = (lane >> 1) & 3;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint64_t x = uint32_t(w[i] >> 32) == ep ? w[i] : flagged_word_gpu(blk + 8 * lane + 2 * ((i >> 1) ^ k) + (i & 1), ep);
+        v[i] = __uint_as_float(uint32_t(x));
     }
 }
 
@@ -350,82 +364,78 @@ __device__ __forceinline__ void tr_fold(const TrArgs &a, const TrPhase *P, uint3
 // summation of act_rms_row: lane l of warp w adds, for its blocks w, w+8,
 // ..., elements 8l..8l+7 (fp32 squares in double), then a warp butterfly,
 // then warps in order.
-__device__ __forceinline__ bool tr_image_rms(const TrArgs &a, const TrPhase *P, uint32_t ep, double *part,
-                                             uint8_t *stg, uint64_t *ibar, uint32_t &iphase, uint8_t *img) {
+__device__ __forceinline__ void tr_image_rms(const TrArgs &a, const TrPhase *P, uint32_t ep, double *part,
+                                             uint8_t *img) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nbk = P->nbk;
     const int64_t k = int64_t(nbk) * kQK_K;
-    const bool ok = tr_stage(a.R, 0, nbk, stg, ibar, iphase);
     const int nbw = nbk > warp ? (nbk - warp + 7) / 8 : 0;
-    const uint64_t *sw = reinterpret_cast<const uint64_t *>(stg);
+    uint64_t w[kTrRmsBlocks][8];
+#pragma unroll
+    for (int jj = 0; jj < kTrRmsBlocks; jj++)
+        if (jj < nbw) tr_load_lane(a.R + int64_t(warp + 8 * jj) * kQK_K, w[jj]);
     float vk[kTrRmsBlocks][8];
     double s = 0.0;
 #pragma unroll
     for (int jj = 0; jj < kTrRmsBlocks; jj++)
         if (jj < nbw) {
-            const int64_t b = warp + 8 * jj;
-            tr_read8(sw + b * kQK_K, a.R + b * kQK_K, ep, vk[jj]);
+            tr_check_lane(a.R + int64_t(warp + 8 * jj) * kQK_K, ep, w[jj], vk[jj]);
 #pragma unroll
             for (int e = 0; e < 8; e++) s += double(__fmul_rn(vk[jj][e], vk[jj][e]));
         }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if (lane == 0) part[warp] = s;
-    __syncthreads();
+    tr_bar();
     double tot = 0.0;
 #pragma unroll
-    for (int w = 0; w < 8; w++) tot += part[w];
+    for (int i = 0; i < 8; i++) tot += part[i];
     const float mean = float(tot / double(k));
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, P->eps)));
     const float *g = P->g;
 #pragma unroll
     for (int jj = 0; jj < kTrRmsBlocks; jj++)
         if (jj < nbw) act_quantize_store(kActRms, vk[jj], scale, g, warp + 8 * jj, 0, k, 1, img);
-    return ok;
 }
 
-// The plain image of a flagged vector (q for o, silu(gate) * up for down),
-// staged kTrStgBlocks blocks at a time.
-__device__ __forceinline__ bool tr_image_vec(const uint64_t *buf, int nbk, uint32_t ep, uint8_t *stg, uint64_t *ibar,
-                                             uint32_t &iphase, uint8_t *img) {
+// The plain image of a flagged vector (q for o, silu(gate) * up for down).
+__device__ __forceinline__ void tr_image_vec(const uint64_t *buf, int nbk, uint32_t ep, uint8_t *img) {
     const int warp = threadIdx.x >> 5;
     const int64_t k = int64_t(nbk) * kQK_K;
-    const uint64_t *sw = reinterpret_cast<const uint64_t *>(stg);
-    bool ok = true;
-    for (int b0 = 0; b0 < nbk; b0 += kTrStgBlocks) {
-        const int nb = nbk - b0 < kTrStgBlocks ? nbk - b0 : kTrStgBlocks;
-        if (b0 > 0) __syncthreads();  // every warp is done with the previous staged blocks
-        ok = tr_stage(buf, b0, nb, stg, ibar, iphase) && ok;
-        for (int j = warp; j < nb; j += 8) {
-            float v[8];
-            tr_read8(sw + int64_t(j) * kQK_K, buf + int64_t(b0 + j) * kQK_K, ep, v);
-            act_quantize_store(kActPlain, v, 1.0f, nullptr, b0 + j, 0, k, 1, img);
-        }
+    for (int b0 = warp; b0 < nbk; b0 += 8 * kTrVecBatch) {
+        uint64_t w[kTrVecBatch][8];
+#pragma unroll
+        for (int jj = 0; jj < kTrVecBatch; jj++)
+            if (b0 + 8 * jj < nbk) tr_load_lane(buf + int64_t(b0 + 8 * jj) * kQK_K, w[jj]);
+#pragma unroll
+        for (int jj = 0; jj < kTrVecBatch; jj++)
+            if (b0 + 8 * jj < nbk) {
+                float v[8];
+                tr_check_lane(buf + int64_t(b0 + 8 * jj) * kQK_K, ep, w[jj], v);
+                act_quantize_store(kActPlain, v, 1.0f, nullptr, b0 + 8 * jj, 0, k, 1, img);
+            }
     }
-    return ok;
 }
 
 __device__ __forceinline__ bool tr_error_set() {
     return (*reinterpret_cast<volatile uint32_t *>(&g_dev_error) & kDevErrWaitTimeout) != 0;
 }
 
-__global__ void __launch_bounds__(kTrWarps * 32, 1) trunk_kernel(const __grid_constant__ TrArgs a) {
+__global__ void __maxnreg__(kTrRegLaunch) trunk_kernel(const __grid_constant__ TrArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * kTrStages;
-    uint64_t *ibar = reinterpret_cast<uint64_t *>(smem + 256);
-    double *part = reinterpret_cast<double *>(smem + 320);
-    uint8_t *stg = smem + kTrHdrBytes;
-    uint8_t *img = stg + kTrStgBytes;
-    uint8_t *ring = img + a.act_bytes + warp * kTrStages * kRowStageBytes;
-    float *red = reinterpret_cast<float *>(img + a.act_bytes + kTrRingBytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);                  // [warp][stage]: the copy landed
+    uint64_t *empty = reinterpret_cast<uint64_t *>(smem + kTrBarBytes);   // [warp][stage]: the warp has read it
+    double *part = reinterpret_cast<double *>(smem + 2 * kTrBarBytes);
+    uint8_t *img = smem + kTrHdrBytes;
+    uint8_t *ring0 = img + a.act_bytes;  // [warp][stage] of kRowStageBytes
+    float *red = reinterpret_cast<float *>(ring0 + kTrRingBytes);
     int *red_cnt = reinterpret_cast<int *>(red + (kRowRedSlots + 1) * kTrWarps * 32);
     int *red_gen = red_cnt + kRowRedSlots + 1;
-    if (lane == 0) {
-#pragma unroll
-        for (int s = 0; s < kTrStages; s++) mbar_init(&bars[s], 1);
+    if (threadIdx.x < kTrWarps * kTrStages) {
+        mbar_init(&full[threadIdx.x], 1);
+        mbar_init(&empty[threadIdx.x], 1);
     }
-    if (threadIdx.x == 0) mbar_init(ibar, 1);
     fence_mbar_init();
     __syncthreads();
 
@@ -433,216 +443,222 @@ __global__ void __launch_bounds__(kTrWarps * 32, 1) trunk_kernel(const __grid_co
     const unsigned E0 = *reinterpret_cast<volatile unsigned *>(a.ctl);
     const unsigned seq0 = a.world > 1 ? *reinterpret_cast<volatile unsigned *>(a.ar_seq) : 0u;
     auto epoch = [&](int p) { return E0 + 2u + unsigned(p); };  // p = -1: the run's input
-    const uint64_t policy = l2_policy_evict_first();
-    uint32_t iphase = 0;
 
-    // ---- issue cursor: this warp's stages of phase ip, then of the following phases ----
-    int ip = a.n_ph;
-    TrRange ir;
-    TrCursor pc;
-    auto i_seek = [&](int from) {
-        for (ip = from; ip < a.n_ph; ip++)
-            if (tr_range(a.ph + ip, c, ir) && warp < ir.L) {
-                tr_seek(ir, pc, warp);
-                return;
+    if (warp >= kTrWarps) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kTrRegCopy));
+        // ---- the copy warp: lane w issues compute warp w's stages, phase after phase ----
+        if (warp == kTrWarps && lane < kTrWarps) {
+            const int w = lane;
+            const uint64_t policy = l2_policy_evict_first();
+            uint8_t *ring = ring0 + w * kTrStages * kRowStageBytes;
+            int ip = a.n_ph;
+            TrRange ir;
+            TrCursor pc;
+            auto i_seek = [&](int from) {
+                for (ip = from; ip < a.n_ph; ip++)
+                    if (tr_range(a.ph + ip, c, ir) && w < ir.L) {
+                        tr_seek(ir, pc, w);
+                        return;
+                    }
+            };
+            i_seek(0);
+            int64_t issued = 0;
+            while (ip < a.n_ph) {
+                const int s = int(issued % kTrStages);
+                if (issued >= kTrStages &&
+                    !mbar_wait_bounded(&empty[w * kTrStages + s], uint32_t(issued / kTrStages - 1) & 1u))
+                    break;  // the compute warp stopped (error recorded)
+                uint64_t *bar = &full[w * kTrStages + s];
+                mbar_arrive_expect_tx(bar, kRowStageBytes);
+                const int x = pc.kb * (kQ4K_Bytes / 8);
+                if (ir.pair) {
+                    const int row0 = int(pc.mb * 16);
+                    tma_load_2d(ring + s * kRowStageBytes, &a.w[ir.w0].tmap, x, row0, bar, policy);
+                    tma_load_2d(ring + s * kRowStageBytes + 16 * kQ4K_Bytes, &a.w[ir.w0 + 1].tmap, x, row0, bar, policy);
+                } else {
+                    const int wi = tr_weight_of(ir, pc.mb);
+                    const int row0 = int((pc.mb - (wi == 0 ? 0 : wi == 1 ? ir.mbs1 : ir.mbs2)) * kRowRows);
+                    tma_load_2d(ring + s * kRowStageBytes, &a.w[ir.w0 + wi].tmap, x, row0, bar, policy);
+                }
+                issued++;
+                tr_advance(ir, pc);
+                if (pc.j >= ir.L) i_seek(ip + 1);
             }
-    };
-    int64_t issued = 0;
-    auto issue = [&](int slot) {
-        if (ip >= a.n_ph) return;
-        if (lane == 0) {
-            mbar_arrive_expect_tx(&bars[slot], kRowStageBytes);
-            const int x = pc.kb * (kQ4K_Bytes / 8);
-            if (ir.pair) {
-                const int row0 = int(pc.mb * 16);
-                tma_load_2d(ring + slot * kRowStageBytes, &a.w[ir.w0].tmap, x, row0, &bars[slot], policy);
-                tma_load_2d(ring + slot * kRowStageBytes + 16 * kQ4K_Bytes, &a.w[ir.w0 + 1].tmap, x, row0, &bars[slot],
-                            policy);
-            } else {
-                const int wi = tr_weight_of(ir, pc.mb);
-                const int row0 = int((pc.mb - (wi == 0 ? 0 : wi == 1 ? ir.mbs1 : ir.mbs2)) * kRowRows);
-                tma_load_2d(ring + slot * kRowStageBytes, &a.w[ir.w0 + wi].tmap, x, row0, &bars[slot], policy);
-            }
+            // the copies still in flight land before the CTA leaves (normally all were read already)
+            for (int64_t u = issued > kTrStages ? issued - kTrStages : 0; u < issued; u++)
+                mbar_wait_bounded(&full[w * kTrStages + int(u % kTrStages)], uint32_t(u / kTrStages) & 1u);
         }
-        issued++;
-        tr_advance(ir, pc);
-        if (pc.j >= ir.L) i_seek(ip + 1);
-    };
-    i_seek(0);
-    for (int s = 0; s < kTrStages; s++) issue(s);
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kTrRegCompute));
+        // ---- the compute warps ----
+        {  // the run's input: h_in -> R (this CTA's slice)
+            const int64_t e = c * a.n_embd / C + threadIdx.x;
+            if (e < (c + 1) * a.n_embd / C) st_relaxed_gpu_u64(a.R + tr_swz(e), flag_word(epoch(-1), a.h_in[e]));
+            tr_bar();
+            if (threadIdx.x == 0) red_relaxed_add_gpu(a.cnt, 1u);
+        }
+        uint8_t *ring = ring0 + warp * kTrStages * kRowStageBytes;
+        int slot = 0;
+        uint32_t phase_bit = 0;
+        for (int p = 0; p < a.n_ph; p++) {
+            const TrPhase *P = a.ph + p;
+            const uint32_t ep = epoch(p);
+            const int err = threadIdx.x == 0 && tr_error_set();
+            if (P->n_fold > 0) tr_fold(a, P, ep, epoch(P->r_prev), seq0);
+            if (tr_bar_or(err)) break;  // an earlier wait gave up: skip the remaining phases
+            if (P->n_fold > 0 && threadIdx.x == 0) red_relaxed_add_gpu(a.cnt + 1 + 2 * p, 1u);
+            TrRange r;
+            if (!tr_range(P, c, r)) continue;
+            const int nbk = r.nbk;
+            const int64_t k = int64_t(nbk) * kQK_K;
 
-    // ---- the run's input: h_in -> R (this CTA's slice) ----
-    {
-        const int64_t e = c * a.n_embd / C + threadIdx.x;
-        if (e < (c + 1) * a.n_embd / C) st_relaxed_gpu_u64(a.R + tr_swz(e), flag_word(epoch(-1), a.h_in[e]));
-        __syncthreads();
-        if (threadIdx.x == 0) red_relaxed_add_gpu(a.cnt, 1u);
-    }
+            // ---- this phase's activation image ----
+            if (threadIdx.x <= kRowRedSlots) red_cnt[threadIdx.x] = 0;
+            const int64_t mbA = r.lo / nbk;      // the row block the range starts in
+            const bool cutA = (r.lo % nbk) != 0;  // ... and whose head is CTA c-1's tail cut
+            if (threadIdx.x < kRowRedSlots)
+                red_gen[threadIdx.x] = (threadIdx.x == 0 && cutA) ? kRowRedSlots : int(threadIdx.x);
+            if (threadIdx.x == 0) tr_wait_count(a.cnt + P->in_cnt, P->in_target);
+            tr_bar();
+            if (P->in_kind == kTrInR)
+                tr_image_rms(a, P, epoch(P->in_pub), part, img);
+            else
+                tr_image_vec(P->in_buf == kTrBufQ ? a.QB : a.AB, nbk, epoch(P->in_pub), img);
+            tr_bar();
 
-    int slot = 0;
-    uint32_t phase_bit = 0;
-    int64_t consumed = 0;
-    for (int p = 0; p < a.n_ph; p++) {
-        const TrPhase *P = a.ph + p;
-        const uint32_t ep = epoch(p);
-        const int err = threadIdx.x == 0 && tr_error_set();
-        if (P->n_fold > 0) tr_fold(a, P, ep, epoch(P->r_prev), seq0);
-        if (__syncthreads_or(err)) break;  // an earlier wait gave up: skip the remaining phases
-        if (P->n_fold > 0 && threadIdx.x == 0) red_relaxed_add_gpu(a.cnt + 1 + 2 * p, 1u);
-        TrRange r;
-        if (!tr_range(P, c, r)) continue;
-        const int nbk = r.nbk;
-        const int64_t k = int64_t(nbk) * kQK_K;
+            const int8_t *xs = reinterpret_cast<const int8_t *>(img);
+            const float *xd = reinterpret_cast<const float *>(img + align_up(size_t(k), 16));
+            const uint8_t *xb = img + align_up(size_t(k), 16) + align_up(size_t(nbk) * 4, 16);
+            const uint32_t ep_rprev = epoch(P->r_prev);
+            auto store_block = [&](int64_t mb, float v) { tr_store(a, P, r, ep, ep_rprev, seq0, mb, v); };
 
-        // ---- this phase's activation image ----
-        if (threadIdx.x <= kRowRedSlots) red_cnt[threadIdx.x] = 0;
-        const int64_t mbA = r.lo / nbk;      // the row block the range starts in
-        const bool cutA = (r.lo % nbk) != 0;  // ... and whose head is CTA c-1's tail cut
-        if (threadIdx.x < kRowRedSlots) red_gen[threadIdx.x] = (threadIdx.x == 0 && cutA) ? kRowRedSlots : int(threadIdx.x);
-        if (threadIdx.x == 0) tr_wait_count(a.cnt + P->in_cnt, P->in_target);
-        __syncthreads();
-        const bool img_ok = P->in_kind == kTrInR
-                                ? tr_image_rms(a, P, epoch(P->in_pub), part, stg, ibar, iphase, img)
-                                : tr_image_vec(P->in_buf == kTrBufQ ? a.QB : a.AB, nbk, epoch(P->in_pub), stg, ibar,
-                                               iphase, img);
-        if (!__syncthreads_and(img_ok)) break;
-
-        const int8_t *xs = reinterpret_cast<const int8_t *>(img);
-        const float *xd = reinterpret_cast<const float *>(img + align_up(size_t(k), 16));
-        const uint8_t *xb = img + align_up(size_t(k), 16) + align_up(size_t(nbk) * 4, 16);
-        const uint32_t ep_rprev = epoch(P->r_prev);
-        auto store_block = [&](int64_t mb, float v) { tr_store(a, P, r, ep, ep_rprev, seq0, mb, v); };
-
-        // ---- compute: the CTA-range split (gemv_row.cuh), one token ----
-        const int64_t L = r.L, LB = r.LB, lo = r.lo, b0 = r.b0;
-        const int fw = int((L - 1) % kTrWarps);
-        const int nw_prev = int(r.lo % nbk < kTrWarps ? r.lo % nbk : kTrWarps);
-        uint64_t *pieces_p = a.pieces + int64_t(p & 1) * C * kTrWarps * 32;
-        const uint64_t *prev = pieces_p + (c - 1) * kTrWarps * 32 + lane;
-        auto finish_cut = [&](const float (&pre)[kTrWarps]) {
-            const int64_t la = ((mbA + 1) * nbk < b0 ? (mbA + 1) * nbk : b0) - lo;
-            const int len = int(la < kTrWarps ? la : kTrWarps);
-            if (!smem_wait_eq(&red_cnt[kRowRedSlots], len)) return;
-            __threadfence_block();
-            float s = 0.0f;
+            // ---- compute: the CTA-range split (gemv_row.cuh), one token ----
+            const int64_t L = r.L, LB = r.LB, lo = r.lo, b0 = r.b0;
+            const int fw = int((L - 1) % kTrWarps);
+            const int nw_prev = int(r.lo % nbk < kTrWarps ? r.lo % nbk : kTrWarps);
+            uint64_t *pieces_p = a.pieces + int64_t(p & 1) * C * kTrWarps * 32;
+            const uint64_t *prev = pieces_p + (c - 1) * kTrWarps * 32 + lane;
+            auto finish_cut = [&](const float (&pre)[kTrWarps]) {
+                const int64_t la = ((mbA + 1) * nbk < b0 ? (mbA + 1) * nbk : b0) - lo;
+                const int len = int(la < kTrWarps ? la : kTrWarps);
+                if (!smem_wait_eq(&red_cnt[kRowRedSlots], len)) return;
+                __threadfence_block();
+                float s = 0.0f;
 #pragma unroll
-            for (int u = 0; u < kTrWarps; u++)
-                if (u < nw_prev) s += pre[u];
-            const int p0 = int(LB % kTrWarps);
+                for (int u = 0; u < kTrWarps; u++)
+                    if (u < nw_prev) s += pre[u];
+                const int p0 = int(LB % kTrWarps);
 #pragma unroll
-            for (int u = 0; u < kTrWarps; u++)
-                if (((u - p0 + kTrWarps) % kTrWarps) < len) s += red[(kRowRedSlots * kTrWarps + u) * 32 + lane];
-            store_block(mbA, s);
-        };
-        auto arrive = [&](int64_t mb, float part_v) -> bool {
-            const int64_t s_it = mb * nbk > lo ? mb * nbk : lo;
-            const int64_t e_it = (mb + 1) * nbk < b0 ? (mb + 1) * nbk : b0;
-            const int len = int(e_it - s_it < kTrWarps ? e_it - s_it : kTrWarps);
-            const int q = int(mb - mbA);
-            if (cutA && q == 0) {
-                red[(kRowRedSlots * kTrWarps + warp) * 32 + lane] = part_v;
+                for (int u = 0; u < kTrWarps; u++)
+                    if (((u - p0 + kTrWarps) % kTrWarps) < len) s += red[(kRowRedSlots * kTrWarps + u) * 32 + lane];
+                store_block(mbA, s);
+            };
+            auto arrive = [&](int64_t mb, float part_v) -> bool {
+                const int64_t s_it = mb * nbk > lo ? mb * nbk : lo;
+                const int64_t e_it = (mb + 1) * nbk < b0 ? (mb + 1) * nbk : b0;
+                const int len = int(e_it - s_it < kTrWarps ? e_it - s_it : kTrWarps);
+                const int q = int(mb - mbA);
+                if (cutA && q == 0) {
+                    red[(kRowRedSlots * kTrWarps + warp) * 32 + lane] = part_v;
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence_block();
+                        atomicAdd(&red_cnt[kRowRedSlots], 1);
+                    }
+                    return true;
+                }
+                const int s = q % kRowRedSlots;
+                if (!smem_wait_eq(&red_gen[s], q)) return false;
+                if (len == 1) {
+                    __syncwarp();
+                    if (lane == 0) *reinterpret_cast<volatile int *>(&red_gen[s]) = q + kRowRedSlots;
+                    store_block(mb, part_v);
+                    return true;
+                }
+                red[(s * kTrWarps + warp) * 32 + lane] = part_v;
                 __syncwarp();
+                int old = 0;
                 if (lane == 0) {
                     __threadfence_block();
-                    atomicAdd(&red_cnt[kRowRedSlots], 1);
+                    old = atomicAdd(&red_cnt[s], 1);
                 }
-                return true;
-            }
-            const int s = q % kRowRedSlots;
-            if (!smem_wait_eq(&red_gen[s], q)) return false;
-            if (len == 1) {
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (old != len - 1) return true;
+                __threadfence_block();
+                const int p0 = int((LB + (s_it - lo)) % kTrWarps);
+                float sum = 0.0f;
+#pragma unroll
+                for (int u = 0; u < kTrWarps; u++)
+                    if (((u - p0 + kTrWarps) % kTrWarps) < len) sum += red[(s * kTrWarps + u) * 32 + lane];
                 __syncwarp();
-                if (lane == 0) *reinterpret_cast<volatile int *>(&red_gen[s]) = q + kRowRedSlots;
-                store_block(mb, part_v);
+                if (lane == 0) {
+                    red_cnt[s] = 0;
+                    __threadfence_block();
+                    *reinterpret_cast<volatile int *>(&red_gen[s]) = q + kRowRedSlots;
+                }
+                store_block(mb, sum);
                 return true;
-            }
-            red[(s * kTrWarps + warp) * 32 + lane] = part_v;
-            __syncwarp();
-            int old = 0;
-            if (lane == 0) {
-                __threadfence_block();
-                old = atomicAdd(&red_cnt[s], 1);
-            }
-            old = __shfl_sync(0xffffffffu, old, 0);
-            if (old != len - 1) return true;
-            __threadfence_block();
-            const int p0 = int((LB + (s_it - lo)) % kTrWarps);
-            float sum = 0.0f;
-#pragma unroll
-            for (int u = 0; u < kTrWarps; u++)
-                if (((u - p0 + kTrWarps) % kTrWarps) < len) sum += red[(s * kTrWarps + u) * 32 + lane];
-            __syncwarp();
-            if (lane == 0) {
-                red_cnt[s] = 0;
-                __threadfence_block();
-                *reinterpret_cast<volatile int *>(&red_gen[s]) = q + kRowRedSlots;
-            }
-            store_block(mb, sum);
-            return true;
-        };
+            };
 
-        float acc = 0.0f;
-        float pre[kTrWarps];
+            float acc = 0.0f;
+            float pre[kTrWarps];
 #pragma unroll
-        for (int u = 0; u < kTrWarps; u++) pre[u] = 0.0f;
-        TrCursor cc;
-        tr_seek(r, cc, warp);
-        bool ok = true;
-        while (cc.j < L) {
-            if (cutA && warp == fw && cc.j + kTrWarps >= L) {  // the finisher's last stage: CTA c-1's words
-                uint64_t w[kTrWarps];
+            for (int u = 0; u < kTrWarps; u++) pre[u] = 0.0f;
+            TrCursor cc;
+            tr_seek(r, cc, warp);
+            bool ok = true;
+            while (cc.j < L) {
+                if (cutA && warp == fw && cc.j + kTrWarps >= L) {  // the finisher's last stage: CTA c-1's words
+                    uint64_t w[kTrWarps];
 #pragma unroll
-                for (int u = 0; u < kTrWarps; u++)
-                    if (u < nw_prev) w[u] = ld_relaxed_gpu_u64(prev + u * 32);
+                    for (int u = 0; u < kTrWarps; u++)
+                        if (u < nw_prev) w[u] = ld_relaxed_gpu_u64(prev + u * 32);
 #pragma unroll
-                for (int u = 0; u < kTrWarps; u++)
-                    if (u < nw_prev)
-                        pre[u] = __uint_as_float(uint32_t(uint32_t(w[u] >> 32) == ep ? w[u]
-                                                                                     : flagged_word_gpu(prev + u * 32, ep)));
-            }
-            if (!mbar_wait_bounded(&bars[slot], phase_bit)) {
-                ok = false;
-                break;
-            }
-            __syncwarp();
-            const uint8_t *blk = ring + slot * kRowStageBytes + lane * kQ4K_Bytes;
-            const uint4 h = *reinterpret_cast<const uint4 *>(blk);
-            uint4 qv[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) qv[i] = *reinterpret_cast<const uint4 *>(blk + 16 + 16 * i);
-            __syncwarp();
-            consumed++;
-            issue(slot);  // the stage is in registers: refill it (possibly with a later phase's weights)
-            float accv[1] = {acc};
-            row_dot<1>(h, qv, xs, xd, xb, k, nbk, cc.kb, accv);
-            acc = accv[0];
-            if (++slot == kTrStages) {
-                slot = 0;
-                phase_bit ^= 1u;
-            }
-            const int64_t mb = cc.mb;
-            const bool in_tail = cc.j < LB;
-            tr_advance(r, cc);
-            if (cc.j >= L || cc.mb != mb) {  // this warp's part of row block mb is complete
-                if (in_tail) {
-                    st_relaxed_gpu_u64(pieces_p + (c * kTrWarps + warp) * 32 + lane, flag_word(ep, acc));
-                } else if (!arrive(mb, acc)) {
+                    for (int u = 0; u < kTrWarps; u++)
+                        if (u < nw_prev)
+                            pre[u] = __uint_as_float(
+                                uint32_t(uint32_t(w[u] >> 32) == ep ? w[u] : flagged_word_gpu(prev + u * 32, ep)));
+                }
+                if (!mbar_wait_bounded(&full[warp * kTrStages + slot], phase_bit)) {
                     ok = false;
                     break;
                 }
-                acc = 0.0f;
+                __syncwarp();
+                const uint8_t *blk = ring + slot * kRowStageBytes + lane * kQ4K_Bytes;
+                const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+                uint4 qv[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) qv[i] = *reinterpret_cast<const uint4 *>(blk + 16 + 16 * i);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[warp * kTrStages + slot]);  // the copy warp may refill it
+                float accv[1] = {acc};
+                row_dot<1>(h, qv, xs, xd, xb, k, nbk, cc.kb, accv);
+                acc = accv[0];
+                if (++slot == kTrStages) {
+                    slot = 0;
+                    phase_bit ^= 1u;
+                }
+                const int64_t mb = cc.mb;
+                const bool in_tail = cc.j < LB;
+                tr_advance(r, cc);
+                if (cc.j >= L || cc.mb != mb) {  // this warp's part of row block mb is complete
+                    if (in_tail) {
+                        st_relaxed_gpu_u64(pieces_p + (c * kTrWarps + warp) * 32 + lane, flag_word(ep, acc));
+                    } else if (!arrive(mb, acc)) {
+                        ok = false;
+                        break;
+                    }
+                    acc = 0.0f;
+                }
             }
+            if (ok && cutA && warp == fw) finish_cut(pre);
+            // this CTA's phase-p outputs are stored; the image and the combination slots are free
+            const int bad = tr_bar_or(!ok);
+            if (threadIdx.x == 0) red_relaxed_add_gpu(a.cnt + 2 + 2 * p, 1u);
+            if (bad) break;
         }
-        if (ok && cutA && warp == fw) finish_cut(pre);
-        // this CTA's phase-p outputs are stored; the image and the combination slots are free
-        const int bad = __syncthreads_or(!ok);
-        if (threadIdx.x == 0) red_relaxed_add_gpu(a.cnt + 2 + 2 * p, 1u);
-        if (bad) break;
     }
 
-    // ---- copies still in flight (normally none: the cursor ends with the last phase) ----
-    for (int64_t u = consumed; u < issued; u++)
-        mbar_wait_bounded(&bars[int(u % kTrStages)], uint32_t(u / kTrStages) & 1u);
     // ---- the last CTA to leave resets the counters, advances the epoch base and the channel's sequence ----
     __shared__ int last;
     __syncthreads();

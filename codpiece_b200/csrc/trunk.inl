@@ -262,7 +262,7 @@ extern "C" cpq_status cpq_trunk_create(const cpq_trunk_layer *layers, int n_laye
     } else {
         ph.back().write_h = 1;  // the last down's residual add
     }
-    const int smem = kTrHdrBytes + kTrStgBytes + act_bytes + kTrRingBytes + row_red_bytes(1);
+    const int smem = kTrHdrBytes + act_bytes + kTrRingBytes + row_red_bytes(1);
     if (smem > kSmemMax)
         return fail(CPQ_ERR_UNSUPPORTED, "cpq_trunk_create: a layer's K is too large (%d B of shared memory)", smem);
 
@@ -287,7 +287,7 @@ extern "C" cpq_status cpq_trunk_create(const cpq_trunk_layer *layers, int n_laye
     e = cudaFuncSetAttribute(trunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return done(cuda_fail(e, "cpq_trunk_create: shared-memory attribute"));
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, trunk_kernel, kTrWarps * 32, size_t(smem));
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, trunk_kernel, kTrThreads, size_t(smem));
     if (e != cudaSuccess || per_sm < 1)
         return done(fail(CPQ_ERR_CUDA, "cpq_trunk_create: the kernel does not fit on an SM"));
     const size_t piece_bytes = size_t(2) * grid * kTrWarps * 32 * sizeof(uint64_t);
@@ -355,7 +355,7 @@ extern "C" cpq_status cpq_trunk_run(cpq_trunk *t, const float *h_in, float *h_ou
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(t->grid));
-    cfg.blockDim = dim3(kTrWarps * 32);
+    cfg.blockDim = dim3(kTrThreads);
     cfg.dynamicSmemBytes = size_t(t->smem);
     cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];

@@ -1,5 +1,7 @@
 """One rank of the tensor-parallel stack check (launched by tests/test_gpu_tp.py
-through torch.distributed.run, one process per GPU).
+through torch.distributed.run, one process per GPU). Modes: "nccl" (per-call
+projections, NCCL all-reduce), "ar" (per-call, fused NVLink all-reduce),
+"trunk" (the persistent trunk kernel, all-reduce inside it).
 
 Every rank builds its shard of a few-layer 27B-shaped stack (split.rs rules,
 NCCL allreduce through libcpq), runs one decode/verify step, and rank 0 also
@@ -25,7 +27,8 @@ def main() -> int:
     out_path = sys.argv[1]
     layers = int(sys.argv[2]) if len(sys.argv) > 2 else 2
     m = int(sys.argv[3]) if len(sys.argv) > 3 else 1
-    fused_ar = len(sys.argv) > 4 and sys.argv[4] == "ar"
+    mode = sys.argv[4] if len(sys.argv) > 4 else "nccl"
+    fused_ar = mode in ("ar", "trunk")
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
@@ -41,7 +44,9 @@ def main() -> int:
         dist.all_gather_object(got, handle)
         return got
 
-    s = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=5, ar_exchange=exchange if fused_ar else None)
+    s = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=5, ar_exchange=exchange if fused_ar else None,
+                 use_trunk=mode == "trunk")
+    assert (s.trunk is not None) == (mode == "trunk")
     assert (s.ar is not None) == fused_ar
     s.h.copy_(h0)
     s.step_body()
@@ -72,7 +77,7 @@ def main() -> int:
         torch.cuda.synchronize()
         lr, hr = ref.logits.cpu().numpy(), ref.h_final.cpu().numpy()
         verdict = {
-            "world": world, "layers": layers, "m": m, "fused_ar": fused_ar,
+            "world": world, "layers": layers, "m": m, "fused_ar": fused_ar, "mode": mode,
             "logits_rel": float(np.abs(logits_tp - lr).max() / np.abs(lr).max()),
             "h_rel": float(np.abs(h_tp - hr).max() / np.abs(hr).max()),
             "tok_tp": tok_tp.tolist(), "tok_ref": ref.tok.cpu().numpy().tolist(),

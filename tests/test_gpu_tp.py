@@ -33,10 +33,12 @@ def _ngpus():
 
 
 @pytest.mark.parametrize("world,layers,m,mode", [(2, 2, 1, "nccl"), (2, 2, 8, "nccl"), (2, 3, 1, "ar"), (2, 2, 3, "ar"),
-                                                 (4, 2, 1, "ar"), (8, 2, 1, "ar"), (8, 2, 8, "nccl")])
+                                                 (2, 3, 1, "trunk"), (4, 2, 1, "ar"), (4, 3, 1, "trunk"),
+                                                 (8, 2, 1, "ar"), (8, 3, 1, "trunk"), (8, 2, 8, "nccl")])
 def test_tensor_parallel_stack_matches_tp1(cuda, tmp_path, world, layers, m, mode):
     """mode "ar": the row-parallel partial sums go through the fused NVLink allreduce
-    (cpq_mul_mat_fused_ar); "nccl": through cpq_tp_allreduce_f32."""
+    (cpq_mul_mat_fused_ar); "nccl": through cpq_tp_allreduce_f32; "trunk": the
+    persistent trunk kernel (cpq_trunk_run) with the all-reduce inside it."""
     if _ngpus() < world:
         pytest.skip(f"needs {world} GPUs")
     out = tmp_path / "verdict.json"
@@ -47,7 +49,7 @@ def test_tensor_parallel_stack_matches_tp1(cuda, tmp_path, world, layers, m, mod
     res = subprocess.run(cmd, cwd=str(ROOT), env=env, capture_output=True, text=True)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     v = json.loads(out.read_text())
-    assert v["fused_ar"] == (mode == "ar")
+    assert v["fused_ar"] == (mode in ("ar", "trunk")) and v["mode"] == mode
     assert v["ranks_agree"]
     assert v["logits_rel"] <= TOL and v["h_rel"] <= TOL, v
     assert v["tok_tp"] == v["tok_ref"], v
