@@ -5,10 +5,11 @@ Workload (every N): the 27B-shaped stack of BASELINE config 5 --
 64 layers of Q4_K q/k/v/o/gate/up/down (hidden 5120, q 6144, kv 1024,
 FFN 17408) plus a mirrored Q6_K head over vocab 151936 -- decoding M = 1
 token per step, tensor-parallel over N GPUs (one process per GPU). Each
-rank's 64 layers run as one persistent trunk kernel (cpq_trunk_run) whose
-row-parallel partial sums cross NVLink inside the kernel; the head is a
-fused Q6_K mul_mat plus argmax. --per-call runs the trunk as one fused call
-per projection instead, --nccl (with --per-call) all-reduces through NCCL.
+projection is one fused call (activation image + decode GEMV) and the
+row-parallel partial sums cross NVLink inside the GEMV (--nccl: through NCCL);
+--trunk runs each rank's 64 layers as one persistent kernel instead
+(cpq_trunk_run, the all-reduce inside it). The head is a fused Q6_K mul_mat
+plus argmax.
 Its FFN projections are exactly BASELINE config 2's Q4_K mat-vec shapes,
 64 times over.
 
@@ -46,8 +47,7 @@ same stack (a few layers per step) and prints the same metric.
 inside an NVTX range named "step" (ncu --nvtx --nvtx-include step/):
   decode_ffn   Q4_K mul_mat M=1 on config 2's gate and down shapes, 2 calls each
   prefill_512  Q4_K mul_mat M=512 on [17408 x 5120], 1 call
-  stack        --steps replays of the captured stack decode step (the trunk kernel at M = 1
-               unless --per-call)
+  stack        --steps replays of the captured stack decode step (--trunk: the trunk kernel)
   head         Q6_K mul_mat on the head [151936 x 5120] at M = 1 and M = 8, 1 call each
 """
 from __future__ import annotations
@@ -439,7 +439,7 @@ def profile_case(args) -> int:
         from codpiece_b200 import stack as st
         from codpiece_b200 import tp
         stack = st.Stack(tp.HP_BENCH_27B, args.layers, 0, 1, None, m=args.m, seed=0,
-                         use_trunk=args.m == 1 and not args.per_call)
+                         use_trunk=args.m == 1 and args.trunk)
         stack.h.copy_(torch.randn(args.m, 5120, device="cuda"))
         stack.capture()
         for _ in range(args.warmup):
@@ -520,8 +520,8 @@ def main() -> int:
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-verify", action="store_true")
     ap.add_argument("--no-small", action="store_true", help="skip the configs[0] / configs[2] lines")
-    ap.add_argument("--nccl", action="store_true", help="with --per-call: TP partial sums through NCCL")
-    ap.add_argument("--per-call", action="store_true", help="one fused call per projection instead of the trunk kernel")
+    ap.add_argument("--nccl", action="store_true", help="TP partial sums through NCCL (not with --trunk)")
+    ap.add_argument("--trunk", action="store_true", help="the persistent trunk kernel instead of one call per projection")
     ap.add_argument("--no-parity", action="store_true", help="skip the N > 1 parity check")
     ap.add_argument("--profile", default=None, choices=["decode_ffn", "prefill_512", "stack", "head"])
     args = ap.parse_args()
@@ -585,7 +585,7 @@ def main() -> int:
             return 3
         torch.cuda.empty_cache()
 
-    use_trunk = args.m == 1 and not args.per_call
+    use_trunk = args.m == 1 and args.trunk
     t_build = time.perf_counter()
     stack = st.Stack(tp.HP_BENCH_27B, args.layers, rank, world, comm, m=args.m, seed=0,
                      ar_exchange=exchange if (world > 1 and not args.nccl) else None, use_trunk=use_trunk)
