@@ -387,6 +387,55 @@ static cudaError_t launch_q6k_rows(const GemvArgs &g, int mt, cudaStream_t st) {
     }
 }
 
+// Q6_K on int8 MMA tiles (gemv_q6k_mma.cuh), up to 16 tokens per weight
+// pass: one weight, dense rows, N a multiple of 8, K <= 30 superblocks. Used
+// from q6m_min_tokens() tokens on (default 2; CPQ_Q6K_MMA_MIN_M overrides:
+// at M = 1 the row-pair kernel streams the head at a similar rate).
+static int q6m_min_tokens() {
+    static const int v = [] {
+        const char *e = std::getenv("CPQ_Q6K_MMA_MIN_M");
+        const int x = e ? std::atoi(e) : 2;
+        return x < 1 ? 1 : x;
+    }();
+    return v;
+}
+
+static bool q6m_ok(const GemvArgs &g, int64_t m) {
+    const int64_t nbk = g.k / kQK_K;
+    const int64_t n = g.row_start[1] - g.row_start[0];
+    return g.n_w == 1 && m >= q6m_min_tokens() && n > 0 && n % 8 == 0 && nbk >= 1 && nbk * kQK_K <= kQ6mMaxK &&
+           g.rs == size_t(nbk) * kQ6K_Bytes && aligned(g.w[0], 16) && q6m_smem_bytes(int(nbk), 16) <= kSmemMax;
+}
+
+template <int MT>
+static cudaError_t launch_q6k_mma_t(const Q6MmaArgs &a, cudaStream_t st) {
+    auto kern = gemv_q6k_mma_kernel<MT>;
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    static std::atomic<int> set[kMaxDevices];
+    if (!set[dev].load(std::memory_order_relaxed)) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+        if (e != cudaSuccess) return e;
+        set[dev].store(1, std::memory_order_relaxed);
+    }
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), a.n / 8));
+    return launch(kern, dim3(unsigned(grid)), dim3(kQ6mWarps * 32), size_t(q6m_smem_bytes(a.nbk, MT)), st, a);
+}
+
+static cudaError_t launch_q6k_mma(const GemvArgs &g, int mt, cudaStream_t st) {
+    Q6MmaArgs a;
+    a.w = g.w[0];
+    a.y = g.y[0];
+    a.y_stride = g.y_stride[0];
+    a.n = g.row_start[1] - g.row_start[0];
+    a.nbk = int(g.k / kQK_K);
+    a.m = mt;
+    a.qs = g.act.qs;
+    a.d = g.act.d;
+    a.bsums = g.act.bsums;
+    return mt <= 8 ? launch_q6k_mma_t<8>(a, st) : launch_q6k_mma_t<16>(a, st);
+}
+
 // Q4_K: fragment-order quantization, then the tensor-core GEMV per group of
 // up to 16 tokens.
 // SM: the activation image goes to shared memory (a.act_smem bytes after the ring).
@@ -838,15 +887,20 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
 
     const uint8_t *base = static_cast<const uint8_t *>(act_ws);
     const int64_t blk = type_blck(vt);
-    for (int64_t t0 = 0; t0 < m; t0 += kGemvMaxTokens) {
-        const int mt = int(std::min<int64_t>(kGemvMaxTokens, m - t0));
+    const bool q6m = s0.wtype == CPQ_TYPE_Q6_K && q6m_ok(a, m);
+    const int64_t group = q6m ? 16 : kGemvMaxTokens;  // tokens per weight pass
+    for (int64_t t0 = 0; t0 < m; t0 += group) {
+        const int mt = int(std::min<int64_t>(group, m - t0));
         GemvArgs g = a;
         g.act.qs = reinterpret_cast<const int8_t *>(base + L.qs_off) + t0 * s0.k;
         g.act.d = reinterpret_cast<const float *>(base + L.d_off) + t0 * (s0.k / blk);
         g.act.bsums = reinterpret_cast<const int16_t *>(base + L.bs_off) + t0 * (s0.k / 16);
         for (int i = 0; i < n_w; i++) g.y[i] = a.y[i] + t0 * a.y_stride[i];
         switch (s0.wtype) {
-        case CPQ_TYPE_Q6_K: e = q6k_rows_ok(g, mt) ? launch_q6k_rows(g, mt, st) : launch_gemv<FmtQ6K>(g, mt, st); break;
+        case CPQ_TYPE_Q6_K:
+            e = q6m ? launch_q6k_mma(g, mt, st) : q6k_rows_ok(g, mt) ? launch_q6k_rows(g, mt, st)
+                                                                     : launch_gemv<FmtQ6K>(g, mt, st);
+            break;
         default: e = q8_rows_ok(g, mt) ? launch_q8_rows(g, mt, st) : launch_gemv<FmtQ8_0>(g, mt, st); break;
         }
         if (e != cudaSuccess) return cuda_fail(e, "gemv launch");

@@ -5,6 +5,7 @@
 //   quantize.cuh     activation re-quantization (Q8_K, Q8_0), bit-exact
 //   gemv.cuh         small-M fused dequant GEMV/GEMM, dp4a (Q6_K, Q8_0)
 //   gemv_q6k.cuh     Q6_K and Q8_0 small-M GEMVs over whole row pairs (LM head, Q8_0 trunk)
+//   gemv_q6k_mma.cuh Q6_K for M <= 16 on int8 MMA tiles of 8 rows (the head in verify)
 //   q8k_block.cuh    the Q8_K block quantizer shared by every Q8_K producer
 //   gemv_mma.cuh     Q4_K verify GEMM (M 4..16) on int8 mma tiles, stream-K
 //   act_prep.cuh     decode activation image: fused rms/swiglu prologue + Q8_K
@@ -35,6 +36,7 @@
 #include "elementwise.cuh"
 #include "gemv.cuh"
 #include "gemv_q6k.cuh"
+#include "gemv_q6k_mma.cuh"
 #include "gemv_mma.cuh"
 #include "act_prep.cuh"
 #include "gemv_row.cuh"

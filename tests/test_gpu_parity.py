@@ -71,6 +71,11 @@ CASES = [
     (synth.Q6_K, 302, 3072, 2),
     (synth.Q6_K, 1000, 5120, 12),
     (synth.Q6_K, 300, 1536, 1),  # K % 1024 != 0: the generic kernel
+    (synth.Q6_K, 4096, 5120, 16),  # int8 MMA tiles of 8 rows, tokens gid and gid + 8
+    (synth.Q6_K, 4096, 5120, 9),
+    (synth.Q6_K, 4104, 7680, 8),   # K at the MMA kernel's limit (30 superblocks)
+    (synth.Q6_K, 64, 256, 2),      # one superblock: a single warp of the CTA has work
+    (synth.Q6_K, 2048, 5120, 33),  # three weight passes of up to 16 tokens
     (synth.Q8_0, 9, 96, 7),
     (synth.Q8_0, 1001, 2080, 1),
     # even N, K % 256 == 0: the Q8_0 row-pair kernel (gemv_q6k.cuh); config 1's shape first
@@ -95,14 +100,14 @@ def test_mul_mat_matches_oracle(cuda, oracle, qt, n, k, m):
 
 
 def test_q6_K_head_full_size(cuda, oracle):
-    """Config 3's Q6_K head [151936 x 5120] at M = 1 and 4, weights made on the device."""
+    """Config 3's Q6_K head [151936 x 5120] at M = 1, 4 and 16, weights made on the device."""
     mm = _mm()
     n, k = 151936, 5120
     w = mm.synth_weights(mm.TYPE_Q6_K, k, n, seed=77)
     w_np = w.data.cpu().numpy()
-    x_np = synth.activations(4, k, seed=78)
+    x_np = synth.activations(16, k, seed=78)
     x = cuda.from_numpy(x_np).cuda()
-    for m in (1, 4):
+    for m in (1, 4, 16):
         y = mm.mul_mat(w, x[:m]).cpu().numpy()
         assert rel_err(y, oracle.mul_mat(oracle.Q6_K, w_np, k, n, x_np[:m])) <= TOL
 
