@@ -389,12 +389,13 @@ static cudaError_t launch_q6k_rows(const GemvArgs &g, int mt, cudaStream_t st) {
 
 // Q6_K on int8 MMA tiles (gemv_q6k_mma.cuh), up to 16 tokens per weight
 // pass: one weight, dense rows, N a multiple of 8, K <= 30 superblocks. Used
-// from q6m_min_tokens() tokens on (default 2; CPQ_Q6K_MMA_MIN_M overrides:
-// at M = 1 the row-pair kernel streams the head at a similar rate).
+// from q6m_min_tokens() tokens on (default 3; CPQ_Q6K_MMA_MIN_M overrides).
+// Measured on the head [151936 x 5120]: 251 us at M = 1..8 against 165 /
+// 222 us for the row-pair kernel at M = 1 / 2 and 285 / 505 us at M = 4 / 8.
 static int q6m_min_tokens() {
     static const int v = [] {
         const char *e = std::getenv("CPQ_Q6K_MMA_MIN_M");
-        const int x = e ? std::atoi(e) : 2;
+        const int x = e ? std::atoi(e) : 3;
         return x < 1 ? 1 : x;
     }();
     return v;
@@ -419,7 +420,7 @@ static cudaError_t launch_q6k_mma_t(const Q6MmaArgs &a, cudaStream_t st) {
         set[dev].store(1, std::memory_order_relaxed);
     }
     const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), a.n / 8));
-    return launch(kern, dim3(unsigned(grid)), dim3(kQ6mWarps * 32), size_t(q6m_smem_bytes(a.nbk, MT)), st, a);
+    return launch(kern, dim3(unsigned(grid)), dim3(q6m_threads(MT)), size_t(q6m_smem_bytes(a.nbk, MT)), st, a);
 }
 
 static cudaError_t launch_q6k_mma(const GemvArgs &g, int mt, cudaStream_t st) {

@@ -14,12 +14,18 @@
 //
 // Tiles. A tile is 8 consecutive weight rows over the whole K: 8 * K/256 *
 // 210 bytes, a multiple of 16 whatever the row alignment, fetched by one bulk
-// copy into a ring of kQ6mStages tile slots shared by the CTA's 8 warps. Warp
-// w takes superblocks [w*nbk/8, (w+1)*nbk/8) of each tile and leaves its fp32
-// partial [16 tokens][8 rows] in a per-slot buffer; the last warp to arrive
-// (shared-memory counter) adds the 8 partials in warp order, stores the rows
-// and refills the slot with the tile kQ6mStages ahead. CTAs take contiguous
-// ranges of tiles.
+// copy into a ring of q6m_stages() tile slots shared by the CTA. For M <= 8
+// the CTA has two teams of 8 warps taking alternate tiles (two warps per
+// scheduler are too few to hide the latency of this kernel's long dependent
+// chains); the ring then has an even number of slots, so the previous tile in
+// a slot always belongs to the same team, whose warps have waited for it: a
+// wait on a slot's barrier is never two phases behind. For M <= 16 the larger
+// activations leave room for three slots and one team. In a team,
+// warp w takes superblocks [w*nbk/8, (w+1)*nbk/8) of the tile and leaves its
+// fp32 partial [16 tokens][8 rows] in a per-slot buffer; the last warp to
+// arrive (shared-memory counter) adds the 8 partials in warp order, stores the
+// rows and refills the slot with the tile kQ6mStages ahead. CTAs take
+// contiguous ranges of tiles.
 //
 // Activations in shared memory (copied once per CTA from the quantizer's
 // image): quants per token row (row stride K + 64 bytes), inside each
@@ -34,9 +40,12 @@
 
 namespace cpq {
 
-constexpr int kQ6mWarps = 8;
+constexpr int kQ6mWarps = 8;   // warps of a team (one tile)
+__host__ __device__ constexpr int q6m_teams(int mt) { return mt <= 8 ? 2 : 1; }
+__host__ __device__ constexpr int q6m_threads(int mt) { return kQ6mWarps * q6m_teams(mt) * 32; }
 constexpr int kQ6mMaxK = 30 * kQK_K;  // 8 rows x 30 superblocks = 50,400 B per tile
 __host__ __device__ constexpr int q6m_stages(int mt) { return mt <= 8 ? 4 : 3; }
+static_assert(q6m_stages(8) % 2 == 0, "two teams need an even ring");
 __host__ __device__ constexpr int q6m_tile_bytes(int nbk) { return 8 * nbk * kQ6K_Bytes; }
 __host__ __device__ constexpr int q6m_qs_stride(int nbk) { return nbk * kQK_K + 64; }
 __host__ __device__ constexpr int q6m_act_bytes(int nbk, int mt) {
@@ -62,18 +71,18 @@ struct Q6MmaArgs {
 
 __device__ __forceinline__ void mma_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0, bool a_unsigned) {
     if (a_unsigned)
-        asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
+        asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
                      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
                      : "r"(a0), "r"(a1), "r"(b0), "r"(0), "r"(0), "r"(0), "r"(0));
     else
-        asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
+        asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
                      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
                      : "r"(a0), "r"(a1), "r"(b0), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
 // A = activations (s8), B = 6-bit quants (u8).
 __device__ __forceinline__ void mma_k16_s8u8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
                  : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
                  : "r"(a0), "r"(a1), "r"(b0), "r"(0), "r"(0), "r"(0), "r"(0));
 }
@@ -183,10 +192,10 @@ __device__ __forceinline__ void q6m_superblock(const uint8_t *tile, int rowb, in
 }
 
 template <int MT>
-__global__ void __launch_bounds__(kQ6mWarps * 32, 1) gemv_q6k_mma_kernel(const __grid_constant__ Q6MmaArgs a) {
+__global__ void __launch_bounds__(q6m_threads(MT), 1) gemv_q6k_mma_kernel(const __grid_constant__ Q6MmaArgs a) {
     constexpr int S = q6m_stages(MT);
     extern __shared__ __align__(128) uint8_t smem[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31, team = int(threadIdx.x >> 5) / kQ6mWarps, warp = int(threadIdx.x >> 5) % kQ6mWarps;
     const int gid = lane >> 2, tig = lane & 3;
     const int nbk = a.nbk;
     const int rowb = nbk * kQ6K_Bytes;
@@ -225,7 +234,7 @@ __global__ void __launch_bounds__(kQ6mWarps * 32, 1) gemv_q6k_mma_kernel(const _
     pdl_launch_dependents();
 
     const int sb0 = warp * nbk / kQ6mWarps, sb1 = (warp + 1) * nbk / kQ6mWarps;
-    for (int64_t t = t0; t < t1; t++) {
+    for (int64_t t = t0 + team; t < t1; t += q6m_teams(MT)) {
         const int64_t i = t - t0;
         const int s = int(i % S);
         if (!mbar_wait_bounded(&full[s], uint32_t(i / S) & 1u)) break;  // error recorded in the device word
