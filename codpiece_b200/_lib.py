@@ -32,7 +32,7 @@ EXPORTED = [
     "cpq_trunk_create", "cpq_trunk_run", "cpq_trunk_phases", "cpq_trunk_destroy",
     "cpq_tp_split_state", "cpq_tp_unique_id", "cpq_tp_comm_init", "cpq_tp_allreduce_f32", "cpq_tp_comm_check",
     "cpq_tp_comm_destroy", "cpq_tp_ar_create", "cpq_tp_ar_connect", "cpq_tp_ar_destroy", "cpq_tp_ar_add", "cpq_tp_ar_zero", "cpq_mul_mat_fused_ar",
-    "cpq_synth_weights", "cpq_device_status", "cpq_last_error", "cpq_status_string",
+    "cpq_synth_weights", "cpq_device_status", "cpq_set_wait_limit_ns", "cpq_last_error", "cpq_status_string",
     "cpq_abi_version",
 ]
 
@@ -124,6 +124,7 @@ def lib() -> C.CDLL:
                                       vp]),
         "cpq_synth_weights": (st, [i32, vp, i64, i64, sz, C.c_uint64, i64, i64, vp]),
         "cpq_device_status": (st, [C.c_int, P(C.c_uint32), C.c_int]),
+        "cpq_set_wait_limit_ns": (st, [C.c_int, C.c_uint64]),
         "cpq_last_error": (C.c_char_p, []),
         "cpq_status_string": (C.c_char_p, [C.c_int]),
         "cpq_abi_version": (C.c_int, []),

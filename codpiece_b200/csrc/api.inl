@@ -1138,6 +1138,18 @@ cpq_status cpq_device_status(int device, uint32_t *err_word, int clear) {
     return *err_word ? fail(CPQ_ERR_DEVICE, "device error word 0x%x", *err_word) : CPQ_SUCCESS;
 }
 
+cpq_status cpq_set_wait_limit_ns(int device, uint64_t ns) {
+    if (device < 0 || device >= kMaxDevices) return fail(CPQ_ERR_INVALID_ARG, "device %d out of range", device);
+    if (ns < 1000ull || ns > 60000000000ull)
+        return fail(CPQ_ERR_INVALID_ARG, "wait limit %llu ns must be in 1 us .. 60 s", (unsigned long long)ns);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof ns);
+    cudaSetDevice(prev);
+    return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "cpq_set_wait_limit_ns");
+}
+
 // ---- NCCL -------------------------------------------------------------------
 
 cpq_status cpq_tp_unique_id(void *id128) {

@@ -35,8 +35,11 @@ enum : uint32_t {
 // One word per device (a __device__ variable has one instance per device).
 __device__ uint32_t g_dev_error;
 
-// Upper bound for any spin on an mbarrier, in nanoseconds of %globaltimer.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// Upper bound for any spin on an mbarrier, a flag or a peer's word, in
+// nanoseconds of %globaltimer: 2 s unless cpq_set_wait_limit_ns changed it
+// (one value per device). Read only after a wait has spun a while.
+__device__ uint64_t g_wait_limit_ns = 2000000000ull;
+__device__ __forceinline__ uint64_t wait_limit_ns() { return *reinterpret_cast<volatile uint64_t *>(&g_wait_limit_ns); }
 
 // ---- PTX helpers -----------------------------------------------------------
 
@@ -79,14 +82,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for phase `parity` of an mbarrier, giving up after kWaitLimitNs.
+// Waits for phase `parity` of an mbarrier, giving up after wait_limit_ns().
 // On give-up it records kDevErrWaitTimeout and returns false.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+        if ((it & 255u) == 0 && global_timer_ns() - t0 > wait_limit_ns()) {
             atomicOr(&g_dev_error, kDevErrWaitTimeout);
             return false;
         }
@@ -252,7 +255,7 @@ __device__ __forceinline__ uint64_t flagged_word_gpu(const uint64_t *p, uint32_t
         w = ld_relaxed_gpu_u64(p);
         if (uint32_t(w >> 32) == flag) return w;
         if ((it & 63u) == 0 && ((*reinterpret_cast<volatile uint32_t *>(&g_dev_error) & kDevErrWaitTimeout) ||
-                                global_timer_ns() - t0 > kWaitLimitNs)) {
+                                global_timer_ns() - t0 > wait_limit_ns())) {
             atomicOr(&g_dev_error, kDevErrWaitTimeout);
             return uint64_t(flag) << 32;
         }
@@ -281,7 +284,7 @@ __device__ __forceinline__ float ar_word(const uint64_t *p, unsigned seq) {
             w = ld_relaxed_sys_u64(p);
             if (unsigned(w >> 32) == seq) break;
             if ((it & 63u) == 0 && ((*reinterpret_cast<volatile uint32_t *>(&g_dev_error) & kDevErrWaitTimeout) ||
-                                    global_timer_ns() - t0 > kWaitLimitNs)) {
+                                    global_timer_ns() - t0 > wait_limit_ns())) {
                 atomicOr(&g_dev_error, kDevErrWaitTimeout);
                 return 0.0f;
             }

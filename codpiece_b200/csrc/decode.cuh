@@ -87,7 +87,7 @@ __device__ __forceinline__ bool grid_wait(const unsigned *bar, unsigned target) 
     const uint64_t t0 = global_timer_ns();
     for (uint32_t it = 1;; ++it) {
         if (ld_acquire_gpu(bar) >= target) return true;
-        if ((it & 63u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+        if ((it & 63u) == 0 && global_timer_ns() - t0 > wait_limit_ns()) {
             atomicOr(&g_dev_error, kDevErrWaitTimeout);
             return false;
         }

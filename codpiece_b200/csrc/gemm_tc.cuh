@@ -47,7 +47,7 @@
 //               After the K loop they read
 //               the CTA's accumulator (tcgen05.ld 32x32b), warps 4-7 the first
 //               half of the token columns, 8-11 the second, and store Y.
-// Waits are bounded (kWaitLimitNs); a timeout sets g_dev_error and a CTA-wide
+// Waits are bounded (wait_limit_ns()); a timeout sets g_dev_error and a CTA-wide
 // abort flag, every role skips to the end, the TMA lanes wait (bounded) for
 // their copies in flight, the MMA lane for its last commit, and the TMEM is
 // released after a cluster barrier. CTAs that start after any wait of the
@@ -236,7 +236,7 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63u) == 0) {
             if (*abort_flag) return false;
-            if (global_timer_ns() - t0 > kWaitLimitNs) {
+            if (global_timer_ns() - t0 > wait_limit_ns()) {
                 atomicOr(&g_dev_error, kDevErrWaitTimeout);
                 *abort_flag = 1;
                 return false;

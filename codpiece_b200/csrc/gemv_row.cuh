@@ -284,7 +284,7 @@ __device__ __forceinline__ bool smem_wait_eq(const int *p, int v) {
     for (uint32_t it = 1;; ++it) {
         if (*reinterpret_cast<const volatile int *>(p) == v) return true;
         if ((it & 63u) == 0 && ((*reinterpret_cast<volatile uint32_t *>(&g_dev_error) & kDevErrWaitTimeout) ||
-                                global_timer_ns() - t0 > kWaitLimitNs)) {
+                                global_timer_ns() - t0 > wait_limit_ns())) {
             atomicOr(&g_dev_error, kDevErrWaitTimeout);
             return false;
         }

@@ -52,7 +52,7 @@
 // Tail-cut words alternate between two halves by phase parity. The last CTA
 // to leave resets the counters for the next run.
 //
-// Every wait is bounded (kWaitLimitNs). After a give-up the device error word
+// Every wait is bounded (wait_limit_ns()). After a give-up the device error word
 // is set, later waits return at once, the CTA skips the remaining phases,
 // waits (bounded) for its copies in flight and exits.
 #pragma once
@@ -169,7 +169,7 @@ __device__ __forceinline__ void tr_wait_count(const unsigned *p, unsigned target
         __nanosleep(32);
         if (ld_relaxed_gpu_u32(p) >= target) return;
         if ((it & 15u) == 0 && ((*reinterpret_cast<volatile uint32_t *>(&g_dev_error) & kDevErrWaitTimeout) ||
-                                global_timer_ns() - t0 > kWaitLimitNs)) {
+                                global_timer_ns() - t0 > wait_limit_ns())) {
             atomicOr(&g_dev_error, kDevErrWaitTimeout);
             return;
         }

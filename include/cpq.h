@@ -386,6 +386,13 @@ cpq_status cpq_synth_weights(int32_t type, void *dst, int64_t n_rows, int64_t n_
  * left set; a caller-provided workspace (cpq_mul_mat_ws) must be re-zeroed
  * by its owner. */
 cpq_status cpq_device_status(int device, uint32_t *err_word, int clear);
+/* Sets how long any device-side wait of the library (a copy's completion, a
+ * neighbouring CTA's words, a peer rank's all-reduce words) may spin before
+ * it gives up and sets the device error word: 2 s by default, here 1 us to
+ * 60 s, for `device` (not while its kernels run). No reference counterpart:
+ * ggml's CUDA backend has no bounded waits; this bounds a stalled or dead
+ * peer. */
+cpq_status cpq_set_wait_limit_ns(int device, uint64_t ns);
 const char *cpq_last_error(void);
 const char *cpq_status_string(cpq_status s);
 int cpq_abi_version(void);

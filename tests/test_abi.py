@@ -154,3 +154,10 @@ def test_trunk_arguments_are_validated_on_the_host(L):
     assert not t.value
     L.cpq_trunk_destroy(None)                                                    # NULL is ignored
     assert L.cpq_trunk_run(None, None, None, None) == 1
+
+
+def test_wait_limit_is_validated_on_the_host(L):
+    assert L.cpq_set_wait_limit_ns(-1, 1_000_000) == 1
+    assert L.cpq_set_wait_limit_ns(0, 10) == 1                 # below 1 us
+    assert L.cpq_set_wait_limit_ns(0, 61_000_000_000) == 1     # above 60 s
+    assert b"wait limit" in L.cpq_last_error()
