@@ -30,6 +30,8 @@ EXPORTED = [
     "cpq_swiglu", "cpq_add_inplace", "cpq_argmax",
     "cpq_decode_plan_create", "cpq_decode_plan_run", "cpq_decode_plan_destroy",
     "cpq_trunk_create", "cpq_trunk_run", "cpq_trunk_phases", "cpq_trunk_destroy",
+    "cpq_gguf_open", "cpq_gguf_close", "cpq_gguf_n_tensors", "cpq_gguf_find_tensor", "cpq_gguf_tensor_at",
+    "cpq_gguf_get_u64", "cpq_gguf_get_str", "cpq_gguf_shard_shape", "cpq_gguf_read_shard", "cpq_gguf_load_shard",
     "cpq_tp_split_state", "cpq_tp_unique_id", "cpq_tp_comm_init", "cpq_tp_allreduce_f32", "cpq_tp_comm_check",
     "cpq_tp_comm_destroy", "cpq_tp_ar_create", "cpq_tp_ar_connect", "cpq_tp_ar_destroy", "cpq_tp_ar_add", "cpq_tp_ar_zero", "cpq_mul_mat_fused_ar",
     "cpq_synth_weights", "cpq_device_status", "cpq_set_wait_limit_ns", "cpq_last_error", "cpq_status_string",
@@ -64,6 +66,11 @@ class CpqDecodePhase(C.Structure):
 class CpqTrunkLayer(C.Structure):
     _fields_ = [(n, C.POINTER(CpqTensor)) for n in ("q", "k", "v", "o", "gate", "up", "down")] + [
         ("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p), ("o_ranks", C.c_uint32)]
+
+
+class CpqGgufTensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("type", C.c_int32), ("n_dims", C.c_int32), ("ne", C.c_int64 * 4),
+                ("offset", C.c_uint64), ("bytes", C.c_uint64)]
 
 
 PRO_NONE, PRO_RMS, PRO_SWIGLU = 0, 1, 2
@@ -109,6 +116,16 @@ def lib() -> C.CDLL:
         "cpq_trunk_run": (st, [vp, vp, vp, vp]),
         "cpq_trunk_phases": (C.c_int, [vp]),
         "cpq_trunk_destroy": (None, [vp]),
+        "cpq_gguf_open": (st, [C.c_char_p, P(vp)]),
+        "cpq_gguf_close": (None, [vp]),
+        "cpq_gguf_n_tensors": (i64, [vp]),
+        "cpq_gguf_find_tensor": (i64, [vp, C.c_char_p]),
+        "cpq_gguf_tensor_at": (st, [vp, i64, P(CpqGgufTensor)]),
+        "cpq_gguf_get_u64": (st, [vp, C.c_char_p, P(C.c_uint64)]),
+        "cpq_gguf_get_str": (st, [vp, C.c_char_p, P(C.c_char_p)]),
+        "cpq_gguf_shard_shape": (st, [vp, i64, P(CpqSplitState), C.c_int, C.c_int, P(i64), P(i64), P(sz)]),
+        "cpq_gguf_read_shard": (st, [vp, i64, P(CpqSplitState), C.c_int, C.c_int, vp, sz]),
+        "cpq_gguf_load_shard": (st, [vp, i64, P(CpqSplitState), C.c_int, C.c_int, vp, sz]),
         "cpq_tp_split_state": (CpqSplitState, [C.c_char_p, P(CpqHparams), i64, i64, C.c_int]),
         "cpq_tp_unique_id": (st, [vp]),
         "cpq_tp_comm_init": (st, [P(vp), C.c_int, C.c_int, vp, C.c_int, C.c_int]),

@@ -22,6 +22,7 @@
 //   plan.inl         cpq_decode_plan_*: host side of the persistent decode kernel
 //   tp_ar.inl        cpq_tp_ar_*: the fused allreduce channel over NVLink peer memory
 //   trunk.inl        cpq_trunk_*: host side of the persistent decode trunk
+//   gguf.inl         cpq_gguf_*: GGUF reader and tensor-parallel shard loader (host)
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ < 1000
 #error "libcpq targets sm_100a (B200) only"
 #endif
@@ -52,3 +53,4 @@
 #include "plan.inl"
 #include "tp_ar.inl"
 #include "trunk.inl"
+#include "gguf.inl"

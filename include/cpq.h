@@ -366,6 +366,47 @@ int cpq_trunk_phases(const cpq_trunk *trunk);
 /* Frees the trunk (after its last run has completed). NULL is ignored. */
 void cpq_trunk_destroy(cpq_trunk *trunk);
 
+/* ---- GGUF files: tensor directory and tensor-parallel shards ---------------
+ *
+ * The reader of crates/codpiece-gguf/src/lib.rs:346-460 (GGUF v1-v3 header,
+ * metadata, tensor directory; no tensor data at open; the same validity
+ * checks: magic, version, count/length caps, power-of-two alignment, every
+ * tensor aligned, in order, non-overlapping and inside the data section) and
+ * the upload half of Weights::load (crates/codpiece-model/src/lib.rs:128-311),
+ * with the tensor-parallel slicing done here on the host: a shard is the part
+ * of a tensor that cpq_tp_split_state assigns to one device (Axis1: whole
+ * rows; Axis0: K ranges of whole quant blocks in every row; MIRRORED or NULL:
+ * the whole tensor), written once as dense rows. */
+typedef struct cpq_gguf cpq_gguf;
+
+typedef struct cpq_gguf_tensor {
+    const char *name;  /* valid while the file handle lives */
+    int32_t type;      /* ggml type id */
+    int32_t n_dims;
+    int64_t ne[4];     /* ne[0] contiguous; unused dimensions 1 */
+    uint64_t offset;   /* absolute byte offset of the data in the file */
+    uint64_t bytes;    /* 0 for a type whose size this library does not know */
+} cpq_gguf_tensor;
+
+cpq_status cpq_gguf_open(const char *path, cpq_gguf **gguf);
+void cpq_gguf_close(cpq_gguf *gguf);
+int64_t cpq_gguf_n_tensors(const cpq_gguf *gguf);
+/* Index of the tensor called name, or -1. */
+int64_t cpq_gguf_find_tensor(const cpq_gguf *gguf, const char *name);
+cpq_status cpq_gguf_tensor_at(const cpq_gguf *gguf, int64_t index, cpq_gguf_tensor *tensor);
+/* Metadata: a non-negative integer value, or a string (valid while the handle lives). */
+cpq_status cpq_gguf_get_u64(const cpq_gguf *gguf, const char *key, uint64_t *value);
+cpq_status cpq_gguf_get_str(const cpq_gguf *gguf, const char *key, const char **value);
+/* Device device_index's shard of a 2-D tensor under split (NULL: the whole
+ * tensor): its ne[0] x ne[1] and byte size, dense rows. */
+cpq_status cpq_gguf_shard_shape(const cpq_gguf *gguf, int64_t index, const cpq_split_state *split, int n_devices,
+                                int device_index, int64_t *ne0, int64_t *ne1, size_t *bytes);
+/* The shard's bytes into host memory, or into device memory (synchronous copy). */
+cpq_status cpq_gguf_read_shard(const cpq_gguf *gguf, int64_t index, const cpq_split_state *split, int n_devices,
+                               int device_index, void *host_dst, size_t dst_bytes);
+cpq_status cpq_gguf_load_shard(const cpq_gguf *gguf, int64_t index, const cpq_split_state *split, int n_devices,
+                               int device_index, void *device_dst, size_t dst_bytes);
+
 /* ---- synthetic weights ----------------------------------------------------- */
 
 /* Fills rows [row0, row0+n_rows) x blocks [blk0, blk0+n_blk) of a tensor of
