@@ -7,8 +7,9 @@ FFN 17408) plus a mirrored Q6_K head over vocab 151936 -- decoding M = 1
 token per step, tensor-parallel over N GPUs (one process per GPU). Each
 projection is one fused call (activation image + decode GEMV) and the
 row-parallel partial sums cross NVLink inside the GEMV (--nccl: through NCCL);
---trunk runs each rank's 64 layers as one persistent kernel instead
-(cpq_trunk_run, the all-reduce inside it). The head is a fused Q6_K mul_mat
+From 4 ranks on (or with --trunk) each rank's 64 layers run as one
+persistent kernel instead (cpq_trunk_run, the all-reduce inside it);
+--per-call keeps one call per projection at every N. The head is a fused Q6_K mul_mat
 plus argmax.
 Its FFN projections are exactly BASELINE config 2's Q4_K mat-vec shapes,
 64 times over.
@@ -521,7 +522,8 @@ def main() -> int:
     ap.add_argument("--no-verify", action="store_true")
     ap.add_argument("--no-small", action="store_true", help="skip the configs[0] / configs[2] lines")
     ap.add_argument("--nccl", action="store_true", help="TP partial sums through NCCL (not with --trunk)")
-    ap.add_argument("--trunk", action="store_true", help="the persistent trunk kernel instead of one call per projection")
+    ap.add_argument("--trunk", action="store_true", help="the persistent trunk kernel at every N")
+    ap.add_argument("--per-call", action="store_true", help="one call per projection at every N")
     ap.add_argument("--no-parity", action="store_true", help="skip the N > 1 parity check")
     ap.add_argument("--profile", default=None, choices=["decode_ffn", "prefill_512", "stack", "head"])
     args = ap.parse_args()
@@ -585,7 +587,9 @@ def main() -> int:
             return 3
         torch.cuda.empty_cache()
 
-    use_trunk = args.m == 1 and args.trunk
+    # default: the trunk kernel from 4 ranks on (there the per-projection launch chain and the
+    # all-reduce waits dominate); one call per projection below, where it is the faster path
+    use_trunk = args.m == 1 and not args.nccl and (args.trunk or (world >= 4 and not args.per_call))
     t_build = time.perf_counter()
     stack = st.Stack(tp.HP_BENCH_27B, args.layers, rank, world, comm, m=args.m, seed=0,
                      ar_exchange=exchange if (world > 1 and not args.nccl) else None, use_trunk=use_trunk)

@@ -27,7 +27,7 @@ STATUS = {
 EXPORTED = [
     "cpq_init", "cpq_release", "cpq_mul_mat_workspace_size", "cpq_mul_mat", "cpq_mul_mat_ws",
     "cpq_mul_mat_multi", "cpq_mul_mat_fused", "cpq_mul_mat_noalloc", "cpq_quantize_act", "cpq_rms_norm",
-    "cpq_swiglu", "cpq_add_inplace", "cpq_argmax",
+    "cpq_swiglu", "cpq_add_inplace", "cpq_argmax", "cpq_gated_delta_net",
     "cpq_decode_plan_create", "cpq_decode_plan_run", "cpq_decode_plan_destroy",
     "cpq_trunk_create", "cpq_trunk_run", "cpq_trunk_phases", "cpq_trunk_destroy",
     "cpq_gguf_open", "cpq_gguf_close", "cpq_gguf_n_tensors", "cpq_gguf_find_tensor", "cpq_gguf_tensor_at",
@@ -109,6 +109,7 @@ def lib() -> C.CDLL:
         "cpq_swiglu": (st, [vp, vp, vp, i64, vp]),
         "cpq_add_inplace": (st, [vp, vp, i64, vp]),
         "cpq_argmax": (st, [vp, i64, i64, vp, vp]),
+        "cpq_gated_delta_net": (st, [P(CpqTensor)] * 7 + [C.c_int32, vp, i64, vp]),
         "cpq_decode_plan_create": (st, [P(CpqDecodePhase), C.c_int, C.c_int, P(vp)]),
         "cpq_decode_plan_run": (st, [vp, vp]),
         "cpq_decode_plan_destroy": (None, [vp]),

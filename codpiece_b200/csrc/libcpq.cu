@@ -13,6 +13,7 @@
 //   gemm_tc.cuh      Q4_K chunked-prefill GEMM (M > 16) on tcgen05 tensor cores
 //   decode.cuh       persistent decode step: a chain of Q4_K GEMV phases in one launch
 //   trunk.cuh        persistent decode trunk: every layer of a rank's step in one launch
+//   gdn.cuh          gated delta-net recurrence (the GDN layers' per-token state update)
 //   elementwise.cuh  rms norm, SwiGLU, residual add, argmax
 //   synth.cuh        seeded synthetic weights
 //   split.inl        tensor-parallel partition rules (host)
@@ -23,6 +24,7 @@
 //   tp_ar.inl        cpq_tp_ar_*: the fused allreduce channel over NVLink peer memory
 //   trunk.inl        cpq_trunk_*: host side of the persistent decode trunk
 //   gguf.inl         cpq_gguf_*: GGUF reader and tensor-parallel shard loader (host)
+//   gdn.inl          cpq_gated_delta_net: host side of gdn.cuh
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ < 1000
 #error "libcpq targets sm_100a (B200) only"
 #endif
@@ -44,6 +46,7 @@
 #include "gemm_tc.cuh"
 #include "decode.cuh"
 #include "trunk.cuh"
+#include "gdn.cuh"
 #include "quantize.cuh"
 #include "synth.cuh"
 #include "split.inl"
@@ -54,3 +57,4 @@
 #include "tp_ar.inl"
 #include "trunk.inl"
 #include "gguf.inl"
+#include "gdn.inl"

@@ -366,6 +366,30 @@ int cpq_trunk_phases(const cpq_trunk *trunk);
 /* Frees the trunk (after its last run has completed). NULL is ignored. */
 void cpq_trunk_destroy(cpq_trunk *trunk);
 
+/* ---- gated delta-net recurrence ---------------------------------------------
+ *
+ * ggml_gated_delta_net as codpiece's GDN layers call it (qwen35.rs:2719;
+ * ggml-cuda gated_delta_net.cu:4-167, replacing ggml_cuda_op_gated_delta_net
+ * and ggml_cuda_op_gated_delta_net_fused_cache, gated_delta_net.cuh:10-14).
+ * Shapes (ggml ne order, F32; q, k, v rows contiguous, the rest contiguous):
+ *   q, k   [S_v, H_qk, T, n_seqs / r]   v head h reads q/k head h % H_qk,
+ *                                       sequence s reads q/k sequence s / r
+ *   v      [S_v, H, T, n_seqs]          S_v = 16, 32, 64 or 128
+ *   g      [1, H, T, n_seqs] (log decay per head) or [S_v, H, T, n_seqs] (per row)
+ *   beta   [1, H, T, n_seqs]
+ *   state  S_v * S_v * H * n_seqs       element (i, col) of head h, sequence s at
+ *                                       ((s * H + h) * S_v + col) * S_v + i
+ * dst: the attention rows [S_v, H, T, n_seqs] (scaled by 1/sqrt(S_v)), then the
+ * state output: with n_snap (the op's K) <= 1 the state after the last token;
+ * with n_snap > 1 slot j (j < min(n_snap, T)) holds the state j tokens before
+ * the last, slots one state set (S_v * S_v * H * n_seqs floats) apart. With
+ * cache non-NULL the state output goes there instead, slots cache_slot_stride
+ * floats apart, and dst needs only the attention rows. state and the state
+ * output may be the same memory. */
+cpq_status cpq_gated_delta_net(const cpq_tensor *q, const cpq_tensor *k, const cpq_tensor *v, const cpq_tensor *g,
+                               const cpq_tensor *beta, const cpq_tensor *state, cpq_tensor *dst, int32_t n_snap,
+                               float *cache, int64_t cache_slot_stride, void *stream);
+
 /* ---- GGUF files: tensor directory and tensor-parallel shards ---------------
  *
  * The reader of crates/codpiece-gguf/src/lib.rs:346-460 (GGUF v1-v3 header,

@@ -134,6 +134,16 @@ int oq_mul_mat_q(int wtype, const void *w, int64_t k, int64_t n, size_t row_stri
 /* Plain fp32 row-dot mul_mat for F32 weights (the smoke.rs layout pin). */
 void oq_mul_mat_f32(const float *w, int64_t k, int64_t n, const float *x, int64_t m, float *y);
 
+/* ggml_gated_delta_net (ggml-cuda gated_delta_net.cu:4-167), contiguous fp32:
+ * q, k [n_seqs_qk][T][H_qk][S_v]; v [n_seqs][T][H][S_v]; g [n_seqs][T][H] (or
+ * [..][H][S_v] when kda); beta [n_seqs][T][H]; state [n_seqs][H][col][i].
+ * attn [n_seqs][T][H][S_v]; state_out: K <= 1 the final state, else slot j
+ * (j < min(K, T)) at state_out + j * slot_stride holds the state j tokens
+ * before the last. In cpq_oracle_gdn.c. Returns 0 or -1. */
+int oq_gated_delta_net(const float *q, const float *k, const float *v, const float *g, const float *beta,
+                       const float *state, float *attn, float *state_out, int64_t sv, int64_t H, int64_t H_qk,
+                       int64_t T, int64_t n_seqs, int64_t n_seqs_qk, int kda, int K, int64_t slot_stride);
+
 /* 1 when the AVX2 build is compiled in. */
 int oq_has_avx2(void);
 int oq_max_threads(void);

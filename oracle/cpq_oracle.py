@@ -24,7 +24,7 @@ _lib = None
 
 
 def build(force: bool = False) -> Path:
-    srcs = [HERE / n for n in ("cpq_oracle.c", "cpq_oracle_avx2.c", "cpq_oracle.h", "Makefile")]
+    srcs = [HERE / n for n in ("cpq_oracle.c", "cpq_oracle_avx2.c", "cpq_oracle_gdn.c", "cpq_oracle.h", "Makefile")]
     if force or not LIB_PATH.exists() or any(s.stat().st_mtime > LIB_PATH.stat().st_mtime for s in srcs):
         env = dict(os.environ)
         env.pop("CC", None)
@@ -55,6 +55,7 @@ def lib() -> C.CDLL:
         L.oq_quantize_row_q8_0.restype = None
         L.oq_quantize_row_q8_K.argtypes = [vp, vp, i64]
         L.oq_quantize_row_q8_K.restype = None
+        L.oq_gated_delta_net.argtypes = [vp] * 8 + [i64] * 6 + [C.c_int, C.c_int, i64]
         _lib = L
     return _lib
 
@@ -131,3 +132,24 @@ def fp32_to_fp16_bits(f: float) -> int:
 
 def max_threads() -> int:
     return int(lib().oq_max_threads())
+
+
+def gated_delta_net(q: np.ndarray, k: np.ndarray, v: np.ndarray, g: np.ndarray, beta: np.ndarray,
+                    state: np.ndarray, n_snap: int = 1):
+    """ggml_gated_delta_net on contiguous arrays (numpy order = ggml ne reversed):
+    q, k [n_seqs_qk, T, H_qk, S_v]; v [n_seqs, T, H, S_v]; g [n_seqs, T, H] or
+    [n_seqs, T, H, S_v] (per-row decay); beta [n_seqs, T, H]; state
+    [n_seqs, H, S_v (col), S_v (i)]. Returns (attn [n_seqs, T, H, S_v],
+    states [slots, n_seqs, H, S_v, S_v]) with slots = min(n_snap, T) (1 if
+    n_snap <= 1)."""
+    q, k, v, g, beta, state = (np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v, g, beta, state))
+    n_seqs, t, h, sv = v.shape
+    n_seqs_qk, _, h_qk, _ = q.shape
+    kda = int(g.ndim == 4)
+    slots = min(n_snap, t) if n_snap > 1 else 1
+    attn = np.empty_like(v)
+    states = np.zeros((slots, n_seqs, h, sv, sv), np.float32)
+    d = n_seqs * h * sv * sv
+    assert lib().oq_gated_delta_net(_p(q), _p(k), _p(v), _p(g), _p(beta), _p(state), _p(attn), _p(states), sv, h,
+                                    h_qk, t, n_seqs, n_seqs_qk, kda, n_snap, d) == 0
+    return attn, states
