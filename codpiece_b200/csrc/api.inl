@@ -664,6 +664,7 @@ static size_t act_region_bytes(int32_t vt, int64_t k, int64_t m) {
         b = std::max(b, size_t(row_act_bytes(k, kRowMaxTokens)));
         b = std::max(b, size_t(m) * size_t(k) * 2);  // fp16 activations of the tensor-core path
     }
+    if (vt == CPQ_TYPE_Q8_0) b = std::max(b, size_t(m) * size_t(k) * 2);
     return align_up(b, 256);
 }
 
@@ -742,19 +743,112 @@ static cudaError_t launch_pair(void (*kern)(KArgs...), dim3 grid, dim3 block, si
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
-// M > 16 (chunked prefill): X is Q8_K-quantized once into fp16 d*q, then each
-// weight runs as one tcgen05 GEMM launch (gemm_tc.cuh) over CTA pairs. Token
-// tiles are as few as possible and balanced (tile_n a multiple of 32, at
-// most 256).
-static cpq_status run_q4k_tc(const GemvArgs &g, const float *x, int64_t x_stride, int64_t m, uint8_t *ws,
-                             cudaStream_t st) {
+// Raw weight rows as a 2-D u64 tensor for the tensor-core GEMM: box = 128 rows x
+// one slot (256 K elements: sb_bytes bytes of each row).
+static cpq_status tc_weight_tensor_map(const uint8_t *w, int64_t n, int64_t nbk, int sb_bytes, size_t rs,
+                                       CUtensorMap *out) {
+    static std::mutex mu;
+    static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> cache;
+    const TmapKey key{w, n, nbk, rs, kTcRows, sb_bytes};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *out = it->second;
+            return CPQ_SUCCESS;
+        }
+    }
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return fail(CPQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {cuuint64_t(nbk) * cuuint64_t(sb_bytes / 8), cuuint64_t(n)};
+    const cuuint64_t strides[1] = {cuuint64_t(rs)};
+    const cuuint32_t box[2] = {cuuint32_t(sb_bytes / 8), cuuint32_t(kTcRows)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUtensorMap m;
+    const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t *>(w), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(CPQ_ERR_CUDA, "cuTensorMapEncodeTiled (weights) failed (%d)", int(r));
+    std::lock_guard<std::mutex> lk(mu);
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, m);
+    *out = m;
+    return CPQ_SUCCESS;
+}
+
+// Q6_K rows as a 2-D u8 tensor whose rows are groups of l weight rows (l * rs
+// bytes, a multiple of 16); box = 240 bytes x 128 / l groups.
+static cpq_status q6_tc_tensor_map(const uint8_t *w, int64_t n, size_t rs, int l, CUtensorMap *out) {
+    static std::mutex mu;
+    static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> cache;
+    const TmapKey key{w, n, int64_t(l), rs, kTcRows, TcW<CPQ_TYPE_Q6_K>::kRowBytes};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *out = it->second;
+            return CPQ_SUCCESS;
+        }
+    }
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return fail(CPQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {cuuint64_t(l) * rs, cuuint64_t(n / l)};
+    const cuuint64_t strides[1] = {cuuint64_t(l) * rs};
+    const cuuint32_t box[2] = {cuuint32_t(TcW<CPQ_TYPE_Q6_K>::kRowBytes), cuuint32_t(kTcRows / l)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUtensorMap m;
+    const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(w), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(CPQ_ERR_CUDA, "cuTensorMapEncodeTiled (Q6_K rows) failed (%d)", int(r));
+    std::lock_guard<std::mutex> lk(mu);
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, m);
+    *out = m;
+    return CPQ_SUCCESS;
+}
+
+// Rows per tensor-map row for Q6_K: the fewest whole rows whose bytes are a multiple of 16.
+static int q6_tc_group(size_t rs) {
+    int l = 1;
+    while (l <= 8 && (size_t(l) * rs) % 16) l *= 2;
+    return l;
+}
+
+// Whether the tensor-core GEMM takes weight type wt with these rows: K whole
+// 256-element slots and 16-byte aligned weights; Q4_K / Q8_0 rows 16-byte
+// aligned for the tensor map; dense Q6_K rows (210-byte superblocks) in
+// groups of L rows whose bytes are 16-byte aligned, N a multiple of L.
+static bool tc_ok(int32_t wt, const GemvArgs &g) {
+    if (g.k % kQK_K) return false;
+    if (wt != CPQ_TYPE_Q4_K && wt != CPQ_TYPE_Q8_0 && wt != CPQ_TYPE_Q6_K) return false;
+    const int l = wt == CPQ_TYPE_Q6_K ? q6_tc_group(g.rs) : 1;
+    if (l > 8 || (wt != CPQ_TYPE_Q6_K && g.rs % 16)) return false;
+    // the Q6_K map spans whole rows of rs bytes, the last one included: dense rows only
+    if (wt == CPQ_TYPE_Q6_K && g.rs != size_t(g.k / kQK_K) * kQ6K_Bytes) return false;
+    for (int i = 0; i < g.n_w; i++)
+        if (!aligned(g.w[i], 16) || (g.row_start[i + 1] - g.row_start[i]) % l) return false;
+    return true;
+}
+
+template <int WT> static void (*tc_kernel())(TcArgs) {
+    return WT == CPQ_TYPE_Q4_K ? gemm_q4k_tc_kernel : WT == CPQ_TYPE_Q8_0 ? gemm_q8_0_tc_kernel : gemm_q6k_tc_kernel;
+}
+
+// M > 16 (chunked prefill): X is quantized once (Q8_K for Q4_K / Q6_K, Q8_0 for
+// Q8_0) into fp16 d*q, then each weight runs as one tcgen05 GEMM launch
+// (gemm_tc.cuh) over CTA pairs. Token tiles are as few as possible and
+// balanced (tile_n a multiple of 32, at most 256).
+template <int WT>
+static cpq_status run_tc(const GemvArgs &g, const float *x, int64_t x_stride, int64_t m, uint8_t *ws, cudaStream_t st) {
     const int64_t k = g.k, nbk = k / kQK_K;
     const int dev = current_device();
     if (dev < 0 || dev >= kMaxDevices) return fail(CPQ_ERR_CUDA, "no current device");
+    auto kern = tc_kernel<WT>();
+    constexpr int smem = tc_smem<WT>();
     static std::atomic<int> set[kMaxDevices];
     if (!set[dev].load(std::memory_order_relaxed)) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(gemm_q4k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core gemm smem attribute");
         set[dev].store(1, std::memory_order_relaxed);
     }
@@ -763,9 +857,16 @@ static cpq_status run_q4k_tc(const GemvArgs &g, const float *x, int64_t x_stride
     if (n_tok_tiles > 65535) return fail(CPQ_ERR_UNSUPPORTED, "M=%lld tokens is too many for one call", (long long)m);
     __half *xh = reinterpret_cast<__half *>(ws + kWsActOffset);
 
-    const int64_t qwarps = m * nbk;
-    cudaError_t e = launch(act_f16_kernel, dim3(unsigned(std::min<int64_t>((qwarps + 7) / 8, 148 * 64))), dim3(256),
-                           0, st, x, k, m, x_stride, xh);
+    cudaError_t e;
+    if (WT == CPQ_TYPE_Q8_0) {
+        const int64_t groups = m * (k / kQK8_0);  // 4 lanes each
+        e = launch(act_f16_q8_0_kernel, dim3(unsigned(std::min<int64_t>((groups + 63) / 64, 148 * 64))), dim3(256), 0,
+                   st, x, k, m, x_stride, xh);
+    } else {
+        const int64_t qwarps = m * nbk;
+        e = launch(act_f16_kernel, dim3(unsigned(std::min<int64_t>((qwarps + 7) / 8, 148 * 64))), dim3(256), 0, st, x,
+                   k, m, x_stride, xh);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "fp16 activation launch");
 
     static thread_local TcArgs a;
@@ -775,13 +876,21 @@ static cpq_status run_q4k_tc(const GemvArgs &g, const float *x, int64_t x_stride
     a.m = m;
     a.nbk = int(nbk);
     a.tile_n = tile_n;
+    a.w_rs = int64_t(g.rs);
     for (int i = 0; i < g.n_w; i++) {
         const int64_t n = g.row_start[i + 1] - g.row_start[i];
         if (n == 0) continue;
         const int64_t pairs = (n + 2 * kTcRows - 1) / (2 * kTcRows);
         if (pairs > (int64_t(1) << 30) / n_tok_tiles)
             return fail(CPQ_ERR_UNSUPPORTED, "N=%lld rows is too many for one call", (long long)n);
-        if ((rc = q4k_tensor_map(g.w[i], n, k, g.rs, &a.tmap_w, kTcRows, 1))) return rc;
+        if (WT == CPQ_TYPE_Q4_K) {
+            if ((rc = q4k_tensor_map(g.w[i], n, k, g.rs, &a.tmap_w, kTcRows, 1))) return rc;
+        } else if (WT == CPQ_TYPE_Q8_0) {
+            if ((rc = tc_weight_tensor_map(g.w[i], n, nbk, TcW<CPQ_TYPE_Q8_0>::kRowBytes, g.rs, &a.tmap_w))) return rc;
+        } else {
+            a.q6_l = q6_tc_group(g.rs);
+            if ((rc = q6_tc_tensor_map(g.w[i], n, g.rs, a.q6_l, &a.tmap_w))) return rc;
+        }
         a.y = g.y[i];
         a.y_stride = g.y_stride[i];
         a.n = n;
@@ -789,7 +898,7 @@ static cpq_status run_q4k_tc(const GemvArgs &g, const float *x, int64_t x_stride
         a.n_tok_tiles = int(n_tok_tiles);
         // persistent: one CTA pair per two SMs (at most one per tile)
         const int64_t grid_pairs = std::min<int64_t>(sm_count(dev) / 2, pairs * n_tok_tiles);
-        e = launch_pair(gemm_q4k_tc_kernel, dim3(unsigned(2 * grid_pairs)), dim3(kTcThreads), size_t(kTcSmem), st, a);
+        e = launch_pair(kern, dim3(unsigned(2 * grid_pairs)), dim3(kTcThreads), size_t(smem), st, a);
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core gemm launch");
     }
     return CPQ_SUCCESS;
@@ -880,7 +989,11 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
         x_stride = s0.k;
     }
     if (s0.wtype == CPQ_TYPE_Q4_K)
-        return m > kMmaMaxTokens ? run_q4k_tc(a, xp, x_stride, m, wsb, st) : run_q4k_mma(a, xp, x_stride, m, wsb, st);
+        return m > kMmaMaxTokens ? run_tc<CPQ_TYPE_Q4_K>(a, xp, x_stride, m, wsb, st)
+                                 : run_q4k_mma(a, xp, x_stride, m, wsb, st);
+    if (m > kTcMinTokens && tc_ok(s0.wtype, a))
+        return s0.wtype == CPQ_TYPE_Q8_0 ? run_tc<CPQ_TYPE_Q8_0>(a, xp, x_stride, m, wsb, st)
+                                         : run_tc<CPQ_TYPE_Q6_K>(a, xp, x_stride, m, wsb, st);
 
     void *act_ws = wsb + kWsActOffset;
     e = launch_quantize(vt, xp, s0.k, m, x_stride, act_ws, L, nullptr, st);

@@ -1,4 +1,8 @@
-// gemm_tc.cuh — Q4_K chunked-prefill GEMM on 5th-generation tensor cores (tcgen05).
+// gemm_tc.cuh — chunked-prefill GEMM on 5th-generation tensor cores (tcgen05)
+// for Q4_K, Q8_0 and Q6_K weights. Written out below for Q4_K; Q8_0 and Q6_K
+// differ only in how a slot of raw weights arrives and how a stage is
+// dequantized (TcW and dq_*_stage), and Q8_0 activations are Q8_0- rather
+// than Q8_K-quantized (act_f16_q8_0_kernel).
 //
 // Y[t][n] = sum_k W[n][k] * X~[t][k] for M > 16 tokens, where
 //   W[n][k] = d*sc_j*q - dmin*m_j     (Q4_K, dequant_row_q4_K in ggml-quants.c)
@@ -67,6 +71,7 @@ constexpr int kTcRows = 128;      // weight rows per CTA (the pair's MMA has M =
 constexpr int kTcMaxTok = 256;    // tokens per pair tile at most (MMA N)
 constexpr int kTcK = 128;         // K elements per stage (two 64-element swizzle atoms)
 constexpr int kTcAtomK = 64;      // K elements per 128-byte swizzle atom
+constexpr int kTcMinTokens = 16;  // Q8_0 / Q6_K products above this many tokens run here
 #ifndef CPQ_TC_A_STAGES
 #define CPQ_TC_A_STAGES 4
 #endif
@@ -78,7 +83,6 @@ constexpr int kTcAtomK = 64;      // K elements per 128-byte swizzle atom
 #endif
 constexpr int kTcAStages = CPQ_TC_A_STAGES;    // dequantized weight stages in TMEM (64 columns each)
 constexpr int kTcBStages = CPQ_TC_B_STAGES;    // activation half-stages in shared memory (32 KB each)
-constexpr int kTcRawSlots = CPQ_TC_RAW_SLOTS;  // raw superblock slots in shared memory (18 KB each)
 constexpr uint32_t kTcAccCols = 256;           // accumulator columns (tile_n <= 256)
 constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcAStageCols = kTcK / 2;  // two fp16 per 32-bit column
@@ -87,16 +91,52 @@ constexpr int kTcThreads = 384;  // 4 role warps + 8 dequantizing warps
 constexpr int kTcDqWarps = 8;
 constexpr int kTcBAtomBytes = kTcMaxTok / 2 * 128;  // one swizzle atom column of the CTA's half
 constexpr int kTcBBytes = kTcBAtomBytes * (kTcK / kTcAtomK);
-constexpr int kTcRawBytes = kTcRows * kQ4K_Bytes;
-constexpr int kTcBarOffset = kTcBStages * kTcBBytes + kTcRawSlots * kTcRawBytes;
-constexpr int kTcBarBytes = int(align_up((2 * (kTcAStages + kTcBStages + kTcRawSlots) + 2) * 8 + 8, 128));
-constexpr int kTcSmem = kTcBarOffset + kTcBarBytes /* barriers, TMEM slot, abort flag */ + 1024 /* alignment slack */;
-static_assert(kTcRawBytes % 1024 == 0 && kTcBBytes % 1024 == 0, "1024-byte stage bases");
-static_assert(kTcSmem <= 227 * 1024, "shared memory");
+
+// The raw weight ring: one slot holds 256 K elements (a Q4_K / Q6_K superblock,
+// eight Q8_0 blocks) of the CTA's 128 rows.
+//   Q4_K  TMA box 128 rows x 144 bytes
+//   Q8_0  TMA box 128 rows x 272 bytes (K a multiple of 256 keeps rows and boxes 16-byte aligned)
+//   Q6_K  210-byte superblocks are only 2-byte aligned and rows rs bytes apart, so the
+//         tensor map's rows are groups of L rows (L * rs the smallest multiple of 16): one
+//         box per member j of the group, 128 / L groups x 240 bytes from the superblock's
+//         start (j * rs + kb * 210 in the group) rounded down to 16. Every row of box j
+//         then has its superblock at the same offset (0..14) inside its 240 bytes, and
+//         bytes past the matrix arrive as zeros. Slot row p holds tile row
+//         L * (p % (128 / L)) + p / (128 / L).
+template <int WT> struct TcW;
+template <> struct TcW<CPQ_TYPE_Q4_K> {
+    static constexpr int kRowBytes = kQ4K_Bytes;
+    static constexpr int kSlots = CPQ_TC_RAW_SLOTS;
+};
+template <> struct TcW<CPQ_TYPE_Q8_0> {
+    static constexpr int kRowBytes = 8 * kQ8_0_Bytes;
+    static constexpr int kSlots = 2;
+};
+template <> struct TcW<CPQ_TYPE_Q6_K> {
+    static constexpr int kRowBytes = 240;
+    static constexpr int kSlots = 3;
+};
+template <int WT> __host__ __device__ constexpr int tc_raw_bytes() { return kTcRows * TcW<WT>::kRowBytes; }
+template <int WT> __host__ __device__ constexpr int tc_bar_offset() { return kTcBStages * kTcBBytes + TcW<WT>::kSlots * tc_raw_bytes<WT>(); }
+template <int WT> constexpr int tc_bar_bytes() {
+    return int(align_up((2 * (kTcAStages + kTcBStages + TcW<WT>::kSlots) + 2) * 8 + 8, 128));
+}
+// barriers, TMEM slot and abort flag after the rings, plus alignment slack
+template <int WT> constexpr int tc_smem() { return tc_bar_offset<WT>() + tc_bar_bytes<WT>() + 1024; }
+static_assert(tc_raw_bytes<CPQ_TYPE_Q4_K>() % 1024 == 0 && tc_raw_bytes<CPQ_TYPE_Q8_0>() % 1024 == 0 &&
+                  tc_raw_bytes<CPQ_TYPE_Q6_K>() % 1024 == 0 && kTcBBytes % 1024 == 0,
+              "1024-byte stage bases");
+static_assert(tc_smem<CPQ_TYPE_Q4_K>() <= 227 * 1024 && tc_smem<CPQ_TYPE_Q8_0>() <= 227 * 1024 &&
+                  tc_smem<CPQ_TYPE_Q6_K>() <= 227 * 1024,
+              "shared memory");
+static_assert(TcW<CPQ_TYPE_Q6_K>::kRowBytes >= kQ6K_Bytes + 14 && TcW<CPQ_TYPE_Q6_K>::kRowBytes % 16 == 0,
+              "Q6_K row window");
 
 struct alignas(64) TcArgs {
     CUtensorMap tmap_x;  // fp16 activations [m][k], box 64 x tile_n/2 (one atom), SWIZZLE_128B
-    CUtensorMap tmap_w;  // Q4_K rows as u64 [n][k/256*18], box 18 x 128
+    CUtensorMap tmap_w;  // Q4_K / Q8_0 rows as u64, box (one slot's bytes / 8) x 128 rows
+    int64_t w_rs;        // Q6_K: bytes between rows
+    int q6_l;            // Q6_K: rows per 16-byte-aligned group (the tensor map's row)
     float *y;            // [m][y_stride]
     int64_t y_stride;
     int64_t n;           // weight rows
@@ -255,6 +295,104 @@ __device__ __forceinline__ __half2 nib2h(uint32_t x) {
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<const uint32_t *>(&h); }
 
+// ---- Q8_0 and Q6_K stages --------------------------------------------------
+//
+// A stage is 128 K elements of one row as 64 fp16x2 TMEM columns (two halves
+// of 32 for tcgen05.st): column 4G + j holds elements 8G + {0,2}, {1,3},
+// {4,6}, {5,7} for j = 0..3, the K order of the activation operand. Weights
+// enter as fp16(s * q) with q exact in fp16 and s the block's fp16 scale
+// (Q8_0: d; Q6_K: fp16(d * sc)), one rounding each.
+
+__device__ __forceinline__ __half2 u32_h2(uint32_t u) { return *reinterpret_cast<const __half2 *>(&u); }
+
+// Bytes b0..b3 of u as fp16 pairs (1024 + b0, 1024 + b2) and (1024 + b1, 1024 + b3), exact.
+__device__ __forceinline__ void bytes_to_h2(uint32_t u, __half2 &e02, __half2 &e13) {
+    e02 = u32_h2(__byte_perm(u, 0x64646464u, 0x4240));
+    e13 = u32_h2(__byte_perm(u, 0x64646464u, 0x4341));
+}
+
+// Blocks 4 GRP .. 4 GRP + 3 of a Q8_0 row slot (8 blocks of 34 bytes).
+template <int GRP>
+__device__ __forceinline__ void dq_q8_0_stage(const uint8_t *row, uint32_t (&v)[2][32]) {
+    uint32_t R[36];  // bytes 128 GRP .. 128 GRP + 143 of the row (16-byte aligned reads)
+#pragma unroll
+    for (int c = 0; c < 9; c++) {
+        const uint4 x = *reinterpret_cast<const uint4 *>(row + 128 * GRP + 16 * c);
+        R[4 * c] = x.x;
+        R[4 * c + 1] = x.y;
+        R[4 * c + 2] = x.z;
+        R[4 * c + 3] = x.w;
+    }
+    const __half2 k1152 = __float2half2_rn(1152.0f);  // 1024 + the 128 that makes q unsigned
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+        const int bo = 8 * GRP + 34 * b;  // the block's first byte in R
+        const uint32_t dh = (R[bo >> 2] >> (8 * (bo & 3))) & 0xffffu;
+        const __half2 d2 = u32_h2(dh | (dh << 16));
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+            const int qo = bo + 2 + 4 * w;
+            const uint32_t q = (qo & 3) ? __byte_perm(R[qo >> 2], R[(qo >> 2) + 1], 0x5432) : R[qo >> 2];
+            __half2 e02, e13;
+            bytes_to_h2(q ^ 0x80808080u, e02, e13);
+            e02 = __hmul2(__hsub2(e02, k1152), d2);
+            e13 = __hmul2(__hsub2(e13, k1152), d2);
+            const int c = 4 * (4 * b + (w >> 1)) + 2 * (w & 1);
+            v[c >> 5][c & 31] = h2u(e02);
+            v[c >> 5][(c & 31) + 1] = h2u(e13);
+        }
+    }
+}
+
+// Half grp of a Q6_K superblock that starts sh bytes into this row's window
+// (dequantize_row_q6_K: elements l + 32 j, l < 32, take ql[l] / ql[l + 32]
+// low or high nibbles, bits 2j..2j+1 of qh[l] and scale sc[l / 16 + 2 j]).
+__device__ __forceinline__ void dq_q6_k_stage(const uint8_t *win, int sh, int grp, uint32_t (&v)[2][32]) {
+    const uint32_t sel = (sh & 2) ? 0x5432u : 0x3210u;  // sh is even: a 0- or 2-byte realignment
+    const uint8_t *base = win + (sh & ~3);
+    // superblock bytes [off, off + 4 n) as n words, from n + 1 aligned reads
+    auto run = [&](int off, uint32_t *out, int n) {
+        const uint32_t *p = reinterpret_cast<const uint32_t *>(base + off);
+        uint32_t prev = p[0];
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            if (i < n) {
+                const uint32_t next = p[i + 1];
+                out[i] = __byte_perm(prev, next, sel);
+                prev = next;
+            }
+    };
+    uint32_t ql[16], qh[8], sc[2];
+    run(64 * grp, ql, 16);
+    run(128 + 32 * grp, qh, 8);
+    run(192 + 8 * grp, sc, 2);
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(win + sh + 208));
+    __half2 s2[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+        s2[i] = __float2half2_rn(d * float(int8_t((sc[i >> 2] >> (8 * (i & 3))) & 0xffu)));
+    const __half2 k1056 = __float2half2_rn(1056.0f);  // 1024 + the 32 of q - 32
+#pragma unroll
+    for (int l4 = 0; l4 < 8; l4++) {
+        const uint32_t L0 = ql[l4], L1 = ql[8 + l4], H = qh[l4];
+        const uint32_t Q[4] = {(L0 & 0x0f0f0f0fu) | ((H << 4) & 0x30303030u), (L1 & 0x0f0f0f0fu) | ((H << 2) & 0x30303030u),
+                               ((L0 >> 4) & 0x0f0f0f0fu) | (H & 0x30303030u),
+                               ((L1 >> 4) & 0x0f0f0f0fu) | ((H >> 2) & 0x30303030u)};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const __half2 sj = s2[(l4 >> 2) + 2 * j];  // elements 4 l4 + 32 j .. + 3 share a 16-group
+            __half2 e02, e13;
+            bytes_to_h2(Q[j], e02, e13);
+            e02 = __hmul2(__hsub2(e02, k1056), sj);
+            e13 = __hmul2(__hsub2(e13, k1056), sj);
+            const int e0 = 4 * l4 + 32 * j;  // first element of the word in the half
+            const int c = 4 * (e0 >> 3) + 2 * ((e0 >> 2) & 1);
+            v[c >> 5][c & 31] = h2u(e02);
+            v[c >> 5][(c & 31) + 1] = h2u(e13);
+        }
+    }
+}
+
 // ---- the kernel -------------------------------------------------------------
 
 // Persistent: grid = 2 x (number of CTA pairs), cluster (2, 1, 1). Pair c
@@ -265,16 +403,18 @@ __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<co
 // accumulator is handed between the MMA issuer and the epilogue with
 // acc_full (multicast commit) and acc_empty (8 epilogue warps of each CTA
 // arrive on rank 0).
-__global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid_constant__ TcArgs a) {
+template <int WT>
+__device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
+    constexpr int kSlots = TcW<WT>::kSlots, kRaw = tc_raw_bytes<WT>();
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sB = smem;
     uint8_t *sRaw = sB + kTcBStages * kTcBBytes;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kTcBarOffset);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + tc_bar_offset<WT>());
     uint64_t *fullA = bars, *emptyA = fullA + kTcAStages;
     uint64_t *fullB = emptyA + kTcAStages, *emptyB = fullB + kTcBStages;
-    uint64_t *rawFull = emptyB + kTcBStages, *rawEmpty = rawFull + kTcRawSlots;
-    uint64_t *acc_full = rawEmpty + kTcRawSlots, *acc_empty = acc_full + 1;
+    uint64_t *rawFull = emptyB + kTcBStages, *rawEmpty = rawFull + kSlots;
+    uint64_t *acc_full = rawEmpty + kSlots, *acc_empty = acc_full + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -297,7 +437,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
             mbar_init(&fullB[s], 1);  // rank 0: its producer's arrive + both halves' bytes
             mbar_init(&emptyB[s], 1);
         }
-        for (int s = 0; s < kTcRawSlots; s++) {
+        for (int s = 0; s < kSlots; s++) {
             mbar_init(&rawFull[s], 1);
             mbar_init(&rawEmpty[s], kTcDqWarps);
         }
@@ -394,33 +534,47 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
         }
         __syncwarp();
     } else if (warp == 2) {
-        // ---- raw Q4_K superblocks (TMA) ----
-        if (lane == 0) {
-            int64_t g = 0;
-            bool ok = true;
-            for (int64_t tile = pair; tile < n_tiles && ok; tile += n_pairs_grid) {
-                const int row0 = int(tile_rows(tile));
-                for (int kb = 0; kb < a.nbk; kb++, g++) {
-                    const int s = int(g % kTcRawSlots);
-                    const uint32_t ph = uint32_t(g / kTcRawSlots) & 1u;
-                    if (*abort_flag || !tc_wait(&rawEmpty[s], ph ^ 1u, abort_flag)) {
-                        ok = false;
-                        break;
+        // ---- raw weights: one slot per 256 K elements of the CTA's 128 rows ----
+        int64_t g = 0;
+        bool ok = true;
+        for (int64_t tile = pair; tile < n_tiles && ok; tile += n_pairs_grid) {
+            const int64_t row0 = tile_rows(tile);
+            for (int kb = 0; kb < a.nbk; kb++, g++) {
+                const int s = int(g % kSlots);
+                const uint32_t ph = uint32_t(g / kSlots) & 1u;
+                int good = 0;
+                if (lane == 0) good = !*abort_flag && tc_wait(&rawEmpty[s], ph ^ 1u, abort_flag);
+                if (!__shfl_sync(0xffffffffu, good, 0)) {
+                    ok = false;
+                    break;
+                }
+                if constexpr (WT == CPQ_TYPE_Q6_K) {
+                    if (lane == 0) {
+                        const int L = a.q6_l, per = kTcRows / L;
+                        mbar_arrive_expect_tx(&rawFull[s], uint32_t(kRaw));
+                        for (int j = 0; j < L; j++)
+                            tma_load_2d(sRaw + s * kRaw + j * per * TcW<WT>::kRowBytes, &a.tmap_w,
+                                        int((int64_t(j) * a.w_rs + int64_t(kb) * kQ6K_Bytes) & ~int64_t(15)),
+                                        int(row0 / L), &rawFull[s]);
                     }
-                    mbar_arrive_expect_tx(&rawFull[s], uint32_t(kTcRawBytes));
-                    tma_load_2d(sRaw + s * kTcRawBytes, &a.tmap_w, kb * (kQ4K_Bytes / 8), row0, &rawFull[s]);
+                } else if (lane == 0) {
+                    mbar_arrive_expect_tx(&rawFull[s], uint32_t(kRaw));
+                    tma_load_2d(sRaw + s * kRaw, &a.tmap_w, kb * (TcW<WT>::kRowBytes / 8), int(row0), &rawFull[s]);
                 }
             }
-            for (int64_t u = g > kTcRawSlots ? g - kTcRawSlots : 0; u < g; u++)
-                mbar_wait_bounded(&rawFull[u % kTcRawSlots], uint32_t(u / kTcRawSlots) & 1u);
         }
+        if (lane == 0)
+            for (int64_t u = g > kSlots ? g - kSlots : 0; u < g; u++)
+                mbar_wait_bounded(&rawFull[u % kSlots], uint32_t(u / kSlots) & 1u);
         __syncwarp();
     } else if (warp >= 4) {
         // ---- dequantization + epilogue (rows past n arrive zero-filled, so they dequantize to 0) ----
         const int dq = warp - 4;
         const int grp = dq >> 2;                      // superblock half (= stage parity) of this warp
         const int quarter = warp & 3;                 // TMEM lane quarter this warp may access
-        const int r = 32 * quarter + lane;            // tile row = TMEM lane
+        const int r = 32 * quarter + lane;            // slot row = TMEM lane
+        // the tile row it holds (Q6_K slots hold the rows grouped by box)
+        const int row_of_lane = WT == CPQ_TYPE_Q6_K ? a.q6_l * (r % (kTcRows / a.q6_l)) + r / (kTcRows / a.q6_l) : r;
         const uint32_t lane_base = uint32_t(32 * quarter) << 16;
         const uint32_t acc_empty0 = cluster_addr(acc_empty, 0);
         int64_t gs = 0;   // stages of all tiles so far (this warp handles those with gs % 2 == grp)
@@ -428,13 +582,40 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
         bool ok = true;
 
         // One stage: dequantize superblock half grp of stage t into A slot gs % kTcAStages.
-        auto dequant_stage = [&](int64_t g_stage, int64_t g_sb) -> bool {
+        // kb: the superblock's index in the row; row0: the tile's first row of this CTA.
+        auto dequant_stage = [&](int64_t g_stage, int64_t g_sb, int kb, int64_t row0) -> bool {
             const int sa = int(g_stage % kTcAStages);
             const uint32_t pa = uint32_t(g_stage / kTcAStages) & 1u;
-            const int rs = int(g_sb % kTcRawSlots);
-            if (!__all_sync(0xffffffffu, tc_wait(&rawFull[rs], uint32_t(g_sb / kTcRawSlots) & 1u, abort_flag)))
+            const int rs = int(g_sb % kSlots);
+            if (!__all_sync(0xffffffffu, tc_wait(&rawFull[rs], uint32_t(g_sb / kSlots) & 1u, abort_flag)))
                 return false;
-            const uint8_t *raw = sRaw + rs * kTcRawBytes + r * kQ4K_Bytes;
+            if constexpr (WT != CPQ_TYPE_Q4_K) {
+                uint32_t v[2][32];
+                const uint8_t *raw = sRaw + rs * kRaw + r * TcW<WT>::kRowBytes;
+                if constexpr (WT == CPQ_TYPE_Q8_0) {
+                    if (grp) dq_q8_0_stage<1>(raw, v);
+                    else dq_q8_0_stage<0>(raw, v);
+                } else {
+                    // where the superblock starts inside this row's window (the copy began 16-aligned)
+                    const int j = r / (kTcRows / a.q6_l);  // the box (member of the row group)
+                    const int sh = int((uint64_t(j) * uint64_t(a.w_rs) + uint64_t(kb) * kQ6K_Bytes) & 15u);
+                    dq_q6_k_stage(raw, sh, grp, v);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&rawEmpty[rs]);  // this warp is done with the slot
+                if (!__all_sync(0xffffffffu, tc_wait(&emptyA[sa], pa ^ 1u, abort_flag))) return false;
+                tc_fence_after();  // the MMAs that read this A stage have completed
+#pragma unroll
+                for (int p = 0; p < 2; p++)
+                    tmem_st32_async(tmem + lane_base + kTcAccCols + kTcAStageCols * uint32_t(sa) + 32u * uint32_t(p),
+                                    v[p]);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(cluster_addr(&fullA[sa], 0));
+                return true;
+            }
+            const uint8_t *raw = sRaw + rs * kRaw + r * kQ4K_Bytes;
             const uint4 hd = *reinterpret_cast<const uint4 *>(raw);
             uint4 qv[4];
 #pragma unroll
@@ -488,7 +669,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
             if (!__all_sync(0xffffffffu, tc_wait(acc_full, uint32_t(it) & 1u, abort_flag))) return false;
             tc_fence_after();
             const int64_t tok0 = tile_tok(tile);
-            const int64_t orow = tile_rows(tile) + r;
+            const int64_t orow = tile_rows(tile) + row_of_lane;
             const int64_t tend = a.m < tok0 + tile_n ? a.m : tok0 + tile_n;
             const int half = (((tile_n + 1) / 2) + 31) & ~31;
             const int cbeg = grp * half, cend = grp ? tile_n : (half < tile_n ? half : tile_n);
@@ -516,9 +697,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
             const int64_t g0 = gs, r0 = gr;
             int t = grp;
             const int prefill = kTcAStages;  // stages of this tile (both groups) before the epilogue
-            for (; t < nk && t < prefill && ok; t += 2) ok = dequant_stage(g0 + t, r0 + (t >> 1));
+            const int64_t row0 = tile_rows(tile);
+            for (; t < nk && t < prefill && ok; t += 2) ok = dequant_stage(g0 + t, r0 + (t >> 1), t >> 1, row0);
             if (ok && prev_tile >= 0) ok = epilogue(prev_tile, it - 1);
-            for (; t < nk && ok; t += 2) ok = dequant_stage(g0 + t, r0 + (t >> 1));
+            for (; t < nk && ok; t += 2) ok = dequant_stage(g0 + t, r0 + (t >> 1), t >> 1, row0);
             gs += nk;
             gr += a.nbk;
             prev_tile = tile;
@@ -532,6 +714,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
     }
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_q4k_tc_kernel(const __grid_constant__ TcArgs a) {
+    gemm_tc_body<CPQ_TYPE_Q4_K>(a);
+}
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_0_tc_kernel(const __grid_constant__ TcArgs a) {
+    gemm_tc_body<CPQ_TYPE_Q8_0>(a);
+}
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_q6k_tc_kernel(const __grid_constant__ TcArgs a) {
+    gemm_tc_body<CPQ_TYPE_Q6_K>(a);
 }
 
 // The tensor-core path's activations: each 256-block of x quantized to Q8_K
@@ -560,6 +752,57 @@ __global__ void __launch_bounds__(256) act_f16_kernel(const float *__restrict__ 
         const uint32_t h[4] = {h2u(__floats2half2_rn(f[0], f[2])), h2u(__floats2half2_rn(f[1], f[3])),
                                h2u(__floats2half2_rn(f[4], f[6])), h2u(__floats2half2_rn(f[5], f[7]))};
         *reinterpret_cast<uint4 *>(out + row * k + b * kQK_K + lane * 8) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+}
+
+// The same for Q8_0 weights: each 32-block of x quantized to Q8_0 exactly as
+// quantize_q8_0_kernel does (the x86 AVX2 semantics: d = fp16(amax / 127),
+// q = round-half-even(x * 127 / amax)), stored as fp16(d * q) in the permuted
+// K order. Four lanes per block, grid-stride over whole warps.
+__global__ void __launch_bounds__(256) act_f16_q8_0_kernel(const float *__restrict__ x, int64_t k, int64_t m,
+                                                           int64_t x_stride, __half *__restrict__ out) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31, sub = lane & 3;
+    const int64_t nb = k / kQK8_0;
+    const int64_t total = m * nb;
+    const int64_t groups_per_iter = int64_t(gridDim.x) * blockDim.x / 4;
+    const int64_t first = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) / 4;
+    for (int64_t base = first - (lane >> 2); base < total; base += groups_per_iter) {
+        const int64_t blk = base + (lane >> 2);
+        const bool valid = blk < total;
+        float v[8];
+        int64_t row = 0, b = 0;
+        if (valid) {
+            row = blk / nb;
+            b = blk - row * nb;
+            const float *xb = x + row * x_stride + b * kQK8_0 + sub * 8;
+            const float4 v0 = *reinterpret_cast<const float4 *>(xb);
+            const float4 v1 = *reinterpret_cast<const float4 *>(xb + 4);
+            v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
+            v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = 0.0f;
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(v[e]));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        if (!valid) continue;
+        const float d = __half2float(__float2half_rn(__fdiv_rn(amax, 127.0f)));
+        const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            int t = __float2int_rn(__fmul_rn(v[e], id));
+            t = t < -128 ? -128 : (t > 127 ? 127 : t);
+            f[e] = __fmul_rn(d, float(t));
+        }
+        const uint32_t h[4] = {h2u(__floats2half2_rn(f[0], f[2])), h2u(__floats2half2_rn(f[1], f[3])),
+                               h2u(__floats2half2_rn(f[4], f[6])), h2u(__floats2half2_rn(f[5], f[7]))};
+        *reinterpret_cast<uint4 *>(out + row * k + b * kQK8_0 + sub * 8) = make_uint4(h[0], h[1], h[2], h[3]);
     }
 }
 
