@@ -48,6 +48,7 @@ same stack (a few layers per step) and prints the same metric.
 inside an NVTX range named "step" (ncu --nvtx --nvtx-include step/):
   decode_ffn   Q4_K mul_mat M=1 on config 2's gate and down shapes, 2 calls each
   prefill_512  Q4_K mul_mat M=512 on [17408 x 5120], 1 call
+  prefill_q8_0_512 / prefill_q6k_512  the same for Q8_0 / Q6_K weights
   stack        --steps replays of the captured stack decode step (--trunk: the trunk kernel)
   head         Q6_K mul_mat on the head [151936 x 5120] at M = 1 and M = 8, 1 call each
 """
@@ -140,18 +141,38 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.rows)}
 
 
+# the sources the decode GEMV (act_prep_kernel + gemv_q4k_row_kernel) is compiled from
+ROW_GEMV_SOURCES = ("common.cuh", "q8k_block.cuh", "act_prep.cuh", "gemv_row.cuh")
+
+
+def source_hash(files=ROW_GEMV_SOURCES) -> str:
+    import hashlib
+    h = hashlib.sha256()
+    for f in files:
+        h.update((ROOT / "codpiece_b200" / "csrc" / f).read_bytes())
+    return h.hexdigest()[:16]
+
+
 def traffic_from_profiles():
-    """Per-launch DRAM bytes of the Q4_K GEMV from the committed ncu summary (or None)."""
+    """Per-launch DRAM bytes of the Q4_K GEMV from the committed ncu summary, used only when the
+    summary was captured from the kernel sources in this tree (its source_sha256 line matches).
+    Returns (bytes or None, note)."""
     p = ROOT / "profiles" / "gemv_q4k_row_ffn.md"
     if not p.exists():
-        return None
+        return None, "no ncu summary"
+    traffic, src = None, None
     for line in p.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
+        t = line.strip()
+        if t.startswith("traffic_bytes_per_launch:"):
             try:
-                return int(line.split(":", 1)[1].strip().split()[0])
+                traffic = int(t.split(":", 1)[1].strip().split()[0])
             except ValueError:
-                return None
-    return None
+                traffic = None
+        elif t.startswith("source_sha256:"):
+            src = t.split(":", 1)[1].strip().split()[0]
+    if src != source_hash():
+        return None, "ncu summary was captured from other kernel sources"
+    return traffic, f"ncu capture of these sources (source_sha256 {src})"
 
 
 def cpu_baseline(seconds: float = 10.0):
@@ -211,10 +232,10 @@ def kernel_roofline(torch, mm, stream, sets: int = 4, reps: int = 20):
     per_op_s = e0.elapsed_time(e1) / 1e3 / (reps * len(ws))
     algo = sum(w.nbytes + 4 * w.k + 4 * w.n for w in ws) / len(ws)
     ach = algo / per_op_s / 1e9
-    traffic = traffic_from_profiles()
+    traffic, traffic_note = traffic_from_profiles()
     del g
     return {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
-            "traffic": traffic, "peak_kind": kind,
+            "traffic": traffic, "traffic_source": traffic_note, "peak_kind": kind,
             "kernel": "Q4_K mul_mat M=1 (act_prep_kernel + gemv_q4k_row_kernel<1>), config 2 shapes",
             "algorithmic_bytes_per_launch": int(algo), "avg_launch_us": round(per_op_s * 1e6, 3),
             "launches_timed": reps * len(ws)}
@@ -249,11 +270,37 @@ def prefill_roofline(torch, mm, reps: int = 10):
     tot_flop = sum(2.0 * c["m"] * c["n"] * c["k"] for c in cases)
     tot_us = sum(c["us"] for c in cases)
     ach = tot_flop / tot_us / 1e6
+    # the same GEMM for the production trunk's Q8_0 and the Q6_K head / fallback at a 512-token chunk
+    others = []
+    for qt, n, k in ((mm.TYPE_Q8_0, 17408, 5120), (mm.TYPE_Q8_0, 5120, 17408), (mm.TYPE_Q6_K, 17408, 5120),
+                     (mm.TYPE_Q6_K, 151936, 5120)):
+        m = 512
+        nw = 1 if n * k > 200_000_000 else 2
+        ws = [mm.synth_weights(qt, k, n, seed=7100 + i) for i in range(nw)]
+        x = torch.randn(m, k, device="cuda")
+        y = torch.empty(m, n, device="cuda")
+        for _ in range(2):
+            for w in ws:
+                mm.mul_mat(w, x, out=y)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        for _ in range(reps):
+            for w in ws:
+                mm.mul_mat(w, x, out=y)
+        e1.record(cur)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * nw)
+        tf = 2.0 * m * n * k / us / 1e6
+        others.append({"type": mm.TYPE_NAMES[qt], "m": m, "n": n, "k": k, "us": round(us, 2), "tflops": round(tf, 1),
+                       "frac": round(tf / peak, 4)})
+        del ws, x, y
     return {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
             "frac": round(ach / peak, 4), "peak_kind": kind,
             "kernel": "Q4_K mul_mat M>16: act_f16_kernel + gemm_q4k_tc_kernel (2-SM tcgen05, fp16 operands, "
                       "fp32 TMEM accumulators)",
-            "achieved_is": "FLOP-weighted over the four configs[3] cases", "best": best, "cases": cases}
+            "achieved_is": "FLOP-weighted over the four configs[3] cases", "best": best, "cases": cases,
+            "q8_0_q6_k_m512": others}
 
 
 def _time_graph(torch, calls, reps: int = 10):
@@ -322,7 +369,35 @@ def small_configs(torch, mm):
                       "head_frac": round(head.nbytes / us_head / 1e3 / hbm, 4)})
         del x, xo, outs, yo, yh
     out["config3_verify_small_m"] = per_m
+    del sets, head
+    out["gdn"] = gdn_recurrence(torch)
     return out
+
+
+def gdn_recurrence(torch):
+    """The GDN recurrence of one 27B GDN layer (48 v heads x 128, 16 q/k heads): T = 1 decode and
+    T = 8 verify with 8 rollback snapshots; state bytes read + written per launch / duration,
+    24 layers' states rotated (> L2)."""
+    from codpiece_b200 import gdn
+    hbm, _ = peaks()
+    res = []
+    for t, n_snap in ((1, 1), (8, 8)):
+        g = torch.Generator(device="cpu").manual_seed(t)
+        q = torch.nn.functional.normalize(torch.randn(1, t, 16, 128, generator=g), dim=-1).cuda()
+        k = torch.nn.functional.normalize(torch.randn(1, t, 16, 128, generator=g), dim=-1).cuda()
+        v = torch.randn(1, t, 48, 128, generator=g).cuda()
+        gg = -torch.rand(1, t, 48, generator=g).cuda()
+        b = torch.rand(1, t, 48, generator=g).cuda()
+        states = [0.1 * torch.randn(1, 48, 128, 128, device="cuda") for _ in range(24)]
+        slots = gdn.state_slots(n_snap, t)
+        outs = [torch.empty(t * 48 * 128 + slots * 48 * 128 * 128, device="cuda") for _ in range(24)]
+        us = _time_graph(torch, [lambda s=s_, o=o_: gdn.gated_delta_net(q, k, v, gg, b, s, n_snap=n_snap, out=o)
+                                 for s_, o_ in zip(states, outs)])
+        byts = 4 * 48 * 128 * 128 * (1 + slots)
+        res.append({"t": t, "k_snap": n_snap, "us": round(us, 2), "state_GBs": round(byts / us / 1e3, 1),
+                    "frac": round(byts / us / 1e3 / hbm, 4)})
+        del states, outs
+    return res
 
 
 def model_bytes(tp, layers: int, head: bool = True) -> int:
@@ -418,6 +493,16 @@ def profile_case(args) -> int:
         nvtx.range_pop()
     elif args.profile == "prefill_512":
         w = mm.synth_weights(mm.TYPE_Q4_K, 5120, 17408, seed=21)
+        x = torch.randn(512, 5120, device="cuda")
+        mm.mul_mat(w, x)
+        torch.cuda.synchronize()
+        nvtx.range_push("step")
+        mm.mul_mat(w, x)
+        torch.cuda.synchronize()
+        nvtx.range_pop()
+    elif args.profile in ("prefill_q8_0_512", "prefill_q6k_512"):
+        qt = mm.TYPE_Q8_0 if args.profile == "prefill_q8_0_512" else mm.TYPE_Q6_K
+        w = mm.synth_weights(qt, 5120, 17408, seed=22)
         x = torch.randn(512, 5120, device="cuda")
         mm.mul_mat(w, x)
         torch.cuda.synchronize()
@@ -525,8 +610,14 @@ def main() -> int:
     ap.add_argument("--trunk", action="store_true", help="the persistent trunk kernel at every N")
     ap.add_argument("--per-call", action="store_true", help="one call per projection at every N")
     ap.add_argument("--no-parity", action="store_true", help="skip the N > 1 parity check")
-    ap.add_argument("--profile", default=None, choices=["decode_ffn", "prefill_512", "stack", "head"])
+    ap.add_argument("--profile", default=None,
+                    choices=["decode_ffn", "prefill_512", "prefill_q8_0_512", "prefill_q6k_512", "stack", "head"])
+    ap.add_argument("--source-hash", action="store_true",
+                    help="print the hash of the decode GEMV's sources (the source_sha256 of its ncu summary)")
     args = ap.parse_args()
+    if args.source_hash:
+        print(source_hash())
+        return 0
     if args.profile:
         return profile_case(args)
     if args.warmup < 3:
