@@ -443,6 +443,7 @@ static cudaError_t launch_q6k_mma(const GemvArgs &g, int mt, cudaStream_t st) {
 template <int NG, bool SM>
 static cudaError_t launch_q4k_mma_t(MmaArgs &a, cudaStream_t st) {
     auto kern = gemv_q4k_mma_kernel<NG, SM>;
+    constexpr int kMmaWarps = MmaCfg<NG>::kWarps;  // this instance's warps per CTA
     const int smem = kMmaSmem + (SM ? a.act_smem : 0);
     const int dev = current_device();
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
@@ -668,8 +669,9 @@ static size_t act_region_bytes(int32_t vt, int64_t k, int64_t m) {
     return align_up(b, 256);
 }
 
+// up != NULL: the input is silu(x) * up, formed inside the quantizer (x = gate rows).
 static cpq_status run_q4k_mma(const GemvArgs &g, const float *x, int64_t x_stride, int64_t m, uint8_t *ws,
-                              cudaStream_t st) {
+                              cudaStream_t st, const float *up = nullptr) {
     const int64_t k = g.k, nbk = k / kQK_K;
     static thread_local MmaArgs a;  // large (tensor maps); filled per call
     std::memset(&a, 0, sizeof a);
@@ -702,7 +704,8 @@ static cpq_status run_q4k_mma(const GemvArgs &g, const float *x, int64_t x_strid
         float *d = reinterpret_cast<float *>(bs + align_up(size_t(nbk) * mp * 16, 256));
         const int64_t qwarps = nbk * mp;
         cudaError_t e = launch(quantize_q8K_frag_kernel, dim3(unsigned(std::min<int64_t>((qwarps + 7) / 8, 65535))),
-                               dim3(256), 0, st, x + t0 * x_stride, k, mt, mp, x_stride, qs, bs, d);
+                               dim3(256), 0, st, x + t0 * x_stride, k, mt, mp, x_stride, qs, bs, d,
+                               up ? up + t0 * x_stride : nullptr);
         if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
         a.m = mt;
         a.act.qs = qs;
@@ -979,11 +982,19 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
     if (s0.wtype == CPQ_TYPE_Q4_K && m <= kRowMaxTokens && row_smem_bytes(s0.k, int(m)) <= kSmemMax)
         return run_q4k_row(a, xp, x_stride, int(m), pro, wsb, st);
 
+    if (pro.mode == CPQ_PRO_SWIGLU && s0.wtype == CPQ_TYPE_Q4_K && m <= kMmaMaxTokens && aligned(xp, 16) &&
+        x_stride % 4 == 0)
+        return run_q4k_mma(a, xp, x_stride, m, wsb, st, pro.r);  // SwiGLU inside the quantizer
     if (pro.mode != CPQ_PRO_NONE) {
         // the other paths quantize an fp32 input: apply the prologue into the workspace first
         float *tmp = reinterpret_cast<float *>(wsb + kWsActOffset + act_region_bytes(vt, s0.k, m));
-        e = launch(prologue_f32_kernel, dim3(unsigned(m)), dim3(256), 0, st, int(pro.mode), xp, pro.r, pro.g,
-                   pro.h_out, x_stride, s0.k, pro.eps, tmp);
+        if (pro.mode == CPQ_PRO_RMS && s0.k % 4 == 0 && s0.k <= kRmsFastMaxK && x_stride % 4 == 0 && aligned(xp, 16) &&
+            (!pro.g || aligned(pro.g, 16)))
+            e = launch(prologue_rms_fast_kernel, dim3(unsigned(m)), dim3(kRmsFastThreads), 0, st, xp, pro.r, pro.g,
+                       pro.h_out, x_stride, s0.k, pro.eps, tmp);
+        else
+            e = launch(prologue_f32_kernel, dim3(unsigned(m)), dim3(256), 0, st, int(pro.mode), xp, pro.r, pro.g,
+                       pro.h_out, x_stride, s0.k, pro.eps, tmp);
         if (e != cudaSuccess) return cuda_fail(e, "prologue launch");
         xp = tmp;
         x_stride = s0.k;

@@ -81,6 +81,73 @@ __global__ void __launch_bounds__(256) prologue_f32_kernel(int mode, const float
     }
 }
 
+// The RMS prologue for rows of k <= kRmsFastMaxK (k % 4 == 0, 16-byte aligned
+// rows): one CTA of 512 threads per row, every load of the row issued at once
+// and kept in registers (thread t holds float4s t, t + 512, ...), so the row
+// costs one memory round trip instead of one per loop step. Same arithmetic
+// as prologue_f32_kernel (fp32 add and square, double sum, fp32 scale),
+// summed per thread, then per warp, then over warps in order.
+constexpr int kRmsFastThreads = 512, kRmsFastVec = 8;
+constexpr int64_t kRmsFastMaxK = int64_t(kRmsFastThreads) * kRmsFastVec * 4;
+__global__ void __launch_bounds__(kRmsFastThreads) prologue_rms_fast_kernel(
+    const float *__restrict__ x, const float *__restrict__ r, const float *__restrict__ g, float *__restrict__ h_out,
+    int64_t x_stride, int64_t k, float eps, float *__restrict__ out) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int64_t row = blockIdx.x;
+    const int64_t n4 = k / 4;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + row * x_stride);
+    const float4 *rr = r ? reinterpret_cast<const float4 *>(r + row * x_stride) : nullptr;
+    float4 v[kRmsFastVec];
+#pragma unroll
+    for (int u = 0; u < kRmsFastVec; u++) {
+        const int64_t i = threadIdx.x + int64_t(u) * kRmsFastThreads;
+        v[u] = i < n4 ? xr[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (rr && i < n4) {
+            const float4 b = rr[i];
+            v[u] = make_float4(__fadd_rn(v[u].x, b.x), __fadd_rn(v[u].y, b.y), __fadd_rn(v[u].z, b.z),
+                               __fadd_rn(v[u].w, b.w));
+        }
+    }
+    double s = 0.0;
+#pragma unroll
+    for (int u = 0; u < kRmsFastVec; u++) {
+        const int64_t i = threadIdx.x + int64_t(u) * kRmsFastThreads;
+        if (i < n4) {
+            if (h_out) reinterpret_cast<float4 *>(h_out + row * x_stride)[i] = v[u];
+            s += double(__fmul_rn(v[u].x, v[u].x));
+            s += double(__fmul_rn(v[u].y, v[u].y));
+            s += double(__fmul_rn(v[u].z, v[u].z));
+            s += double(__fmul_rn(v[u].w, v[u].w));
+        }
+    }
+    __shared__ double part[kRmsFastThreads / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    double tot = 0.0;
+#pragma unroll
+    for (int w = 0; w < kRmsFastThreads / 32; w++) tot += part[w];
+    const float mean = float(tot / double(k));
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    float4 *orow = reinterpret_cast<float4 *>(out + row * k);
+    const float4 *g4 = reinterpret_cast<const float4 *>(g);
+#pragma unroll
+    for (int u = 0; u < kRmsFastVec; u++) {
+        const int64_t i = threadIdx.x + int64_t(u) * kRmsFastThreads;
+        if (i < n4) {
+            float4 o = make_float4(__fmul_rn(v[u].x, scale), __fmul_rn(v[u].y, scale), __fmul_rn(v[u].z, scale),
+                                   __fmul_rn(v[u].w, scale));
+            if (g) {
+                const float4 gg = g4[i];
+                o = make_float4(__fmul_rn(o.x, gg.x), __fmul_rn(o.y, gg.y), __fmul_rn(o.z, gg.z), __fmul_rn(o.w, gg.w));
+            }
+            orow[i] = o;
+        }
+    }
+}
+
 // ggml silu(x) = x / (1 + exp(-x)); act = silu(gate) * up.
 __global__ void swiglu_kernel(const float *__restrict__ gate, const float *__restrict__ up, float *__restrict__ act,
                               int64_t n) {

@@ -50,8 +50,17 @@ constexpr int kMmaStages = CPQ_MMA_STAGES;
 constexpr int kMmaRows = 16;
 constexpr int kMmaPitch = kMmaSB * kQ4K_Bytes;
 constexpr int kMmaStageBytes = kMmaRows * kMmaPitch;
-constexpr int kMmaBarBytes = 128 * ((kMmaWarps * kMmaStages * 8 + 8 + 127) / 128);  // + the activation barrier
-constexpr int kMmaSmem = kMmaBarBytes + kMmaWarps * kMmaStages * kMmaStageBytes;
+__host__ __device__ constexpr int mma_bar_bytes(int w, int st) { return 128 * ((w * st * 8 + 8 + 127) / 128); }  // + the activation barrier
+__host__ __device__ constexpr int mma_smem(int w, int st) { return mma_bar_bytes(w, st) + w * st * kMmaStageBytes; }
+constexpr int kMmaSmem = mma_smem(kMmaWarps, kMmaStages);
+// Per instance: for M <= 8 (one token group) more warps with shallower rings
+// keep more rows in flight per SM (FFN shapes at M = 8: 51.3 vs 58.2 us);
+// for M <= 16 the register-heavier two-group tiles keep 8 warps x 4 stages.
+template <int NG> struct MmaCfg {
+    static constexpr int kWarps = NG == 1 ? 16 : kMmaWarps;
+    static constexpr int kStages = NG == 1 ? 2 : kMmaStages;
+};
+static_assert(mma_smem(16, 2) == kMmaSmem, "every instance has the same ring bytes");
 constexpr int kMmaMaxTokens = 16;
 static_assert(kMmaPitch % 128 == 32, "fragment loads of rows gid..gid+3 must hit distinct bank groups");
 
@@ -234,17 +243,18 @@ __device__ __forceinline__ void q4k_superblock(const uint8_t *p0, const uint8_t 
 // SM: the activation image is copied into shared memory (a.act_smem bytes,
 // after the ring) once per CTA, so the per-superblock fragment loads do not
 // wait on L2.
-template <int NG, bool SM>  // token groups of 8 (1: M <= 8, 2: M <= 16)
-__global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __grid_constant__ MmaArgs a) {
+// W warps of S ring stages each (W * S stages per CTA in all instances).
+template <int NG, bool SM, int W = MmaCfg<NG>::kWarps, int S = MmaCfg<NG>::kStages>  // token groups of 8 (1: M <= 8, 2: M <= 16)
+__global__ void __launch_bounds__(W * 32) gemv_q4k_mma_kernel(const __grid_constant__ MmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gid = lane >> 2, tig = lane & 3;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * kMmaStages;
-    uint64_t *act_bar = reinterpret_cast<uint64_t *>(smem) + kMmaWarps * kMmaStages;
-    uint8_t *ring = smem + kMmaBarBytes + warp * kMmaStages * kMmaStageBytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * S;
+    uint64_t *act_bar = reinterpret_cast<uint64_t *>(smem) + W * S;
+    uint8_t *ring = smem + mma_bar_bytes(W, S) + warp * S * kMmaStageBytes;
     if (lane == 0) {
 #pragma unroll
-        for (int s = 0; s < kMmaStages; s++) mbar_init(&bars[s], 1);
+        for (int s = 0; s < S; s++) mbar_init(&bars[s], 1);
         if (SM && warp == 0) mbar_init(act_bar, 1);
         fence_mbar_init();
     }
@@ -253,7 +263,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __gr
     const int nbk = a.nbk;
     const int64_t T = a.mb_start[a.n_w] * nbk;
     const int64_t G = a.n_warps;
-    const int64_t g = int64_t(blockIdx.x) * kMmaWarps + warp;
+    const int64_t g = int64_t(blockIdx.x) * W + warp;
     if (g >= G) return;  // the grid is rounded up to whole CTAs
     const int64_t it_begin = g * T / G, it_end = (g + 1) * T / G;
     const uint64_t policy = l2_policy_evict_first();
@@ -287,14 +297,14 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __gr
             p_mb++;
         }
     };
-    for (int j = 0; j < kMmaStages && p_it < it_end; j++) issue(j);
+    for (int j = 0; j < S && p_it < it_end; j++) issue(j);
 
     pdl_wait();
     pdl_launch_dependents();
     ActFrag act = a.act;
     if (SM) {
         // the activation image (quants, split 32-sums, scales) into shared memory after the ring
-        uint8_t *as = smem + kMmaSmem;
+        uint8_t *as = smem + mma_smem(W, S);
         const uint32_t qb = uint32_t(nbk) * uint32_t(act.mp) * 256u, bb = uint32_t(nbk) * uint32_t(act.mp) * 16u;
         const uint32_t db = uint32_t(align_up(size_t(nbk) * act.mp * 4, 16));
         if (threadIdx.x == 0) {
@@ -332,9 +342,9 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __gr
             // error recorded in the device word: wait (bounded) for the other copies
             // this warp still has in flight into its ring, then leave
             const int64_t pending = (p_it - c_it) > 0 ? 1 : 0;
-            for (int k2 = 1; k2 < kMmaStages && pending; k2++) {
-                const int sl = (slot + k2) % kMmaStages;
-                mbar_wait_bounded(&bars[sl], phase ^ uint32_t(slot + k2 >= kMmaStages));
+            for (int k2 = 1; k2 < S && pending; k2++) {
+                const int sl = (slot + k2) % S;
+                mbar_wait_bounded(&bars[sl], phase ^ uint32_t(slot + k2 >= S));
             }
             return;
         }
@@ -361,7 +371,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __gr
         if (p_it < it_end) issue(slot);
         c_it += n;
         c_kb += n;
-        if (++slot == kMmaStages) {
+        if (++slot == S) {
             slot = 0;
             phase ^= 1u;
         }
@@ -468,9 +478,12 @@ __global__ void __launch_bounds__(kMmaWarps * 32) gemv_q4k_mma_kernel(const __gr
 // Quantize fp32 rows to Q8_K in fragment order (see ActFrag), padding the
 // token dimension to mp with zeros. One warp per (superblock, token), the
 // same arithmetic as quantize_q8K_kernel.
+// up != NULL: the quantized row is silu(x) * up (the SwiGLU before ffn_down,
+// ggml's silu x / (1 + exp(-x)) then the product), up with x's row stride.
 __global__ void __launch_bounds__(256) quantize_q8K_frag_kernel(const float *__restrict__ x, int64_t k, int m, int mp,
                                                                 int64_t x_stride, int8_t *__restrict__ qs,
-                                                                uint8_t *__restrict__ bs, float *__restrict__ dout) {
+                                                                uint8_t *__restrict__ bs, float *__restrict__ dout,
+                                                                const float *__restrict__ up) {
     pdl_wait();
     pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
@@ -487,6 +500,14 @@ __global__ void __launch_bounds__(256) quantize_q8K_frag_kernel(const float *__r
             const float4 v1 = *reinterpret_cast<const float4 *>(xb + 4);
             v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
             v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
+            if (up) {
+                const float *ub = up + t * x_stride + b * kQK_K + lane * 8;
+                const float4 u0 = *reinterpret_cast<const float4 *>(ub);
+                const float4 u1 = *reinterpret_cast<const float4 *>(ub + 4);
+                const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+                for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fdiv_rn(v[e], __fadd_rn(1.0f, expf(-v[e]))), u[e]);
+            }
         } else {
 #pragma unroll
             for (int e = 0; e < 8; e++) v[e] = 0.0f;
