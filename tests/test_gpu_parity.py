@@ -195,7 +195,7 @@ def test_elementwise_ops_match_reference(cuda):
     assert mm.argmax(t).cpu().tolist() == [1, 0]
 
 
-@pytest.mark.parametrize("m", [1, 3, 8, 64])
+@pytest.mark.parametrize("m", [1, 3, 8, 13, 16, 64])
 def test_fused_prologues_match_oracle(cuda, oracle, m):
     """cpq_mul_mat_fused: rms_norm(x + r) * g and silu(x) * r before quantization."""
     from oracle import stack_ref
