@@ -49,6 +49,7 @@ inside an NVTX range named "step" (ncu --nvtx --nvtx-include step/):
   decode_ffn   Q4_K mul_mat M=1 on config 2's gate and down shapes, 2 calls each
   prefill_512  Q4_K mul_mat M=512 on [17408 x 5120], 1 call
   prefill_q8_0_512 / prefill_q6k_512  the same for Q8_0 / Q6_K weights
+  verify_ffn   Q4_K mul_mat M=8 on config 2's gate and down shapes, 1 call each
   stack        --steps replays of the captured stack decode step (--trunk: the trunk kernel)
   head         Q6_K mul_mat on the head [151936 x 5120] at M = 1 and M = 8, 1 call each
 """
@@ -510,6 +511,17 @@ def profile_case(args) -> int:
         mm.mul_mat(w, x)
         torch.cuda.synchronize()
         nvtx.range_pop()
+    elif args.profile == "verify_ffn":
+        calls = [(mm.synth_weights(mm.TYPE_Q4_K, k, n, seed=41 + i), torch.randn(8, k, device="cuda"))
+                 for i, (n, k) in enumerate(((17408, 5120), (5120, 17408)))]
+        for w, x in calls:
+            mm.mul_mat(w, x)
+        torch.cuda.synchronize()
+        nvtx.range_push("step")
+        for w, x in calls:
+            mm.mul_mat(w, x)
+        torch.cuda.synchronize()
+        nvtx.range_pop()
     elif args.profile == "head":
         w = mm.synth_weights(mm.TYPE_Q6_K, 5120, 151936, seed=31)
         xs = [torch.randn(m, 5120, device="cuda") for m in (1, 8)]
@@ -583,7 +595,12 @@ def reference_arm(args, rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8 dots, fp32 accumulate", "data": "synthetic",
             "config": {"workload": f"27B-shaped Q4_K stack decode, sample of {args.ref_layers} layers per step "
-                                   f"(no head), M={args.m}", "layers_per_step": args.ref_layers, "m": args.m},
+                                   f"(no head), M={args.m}", "layers_per_step": args.ref_layers, "m": args.m,
+                       "same_config": False,
+                       "comparability": "weight GB/s of the same per-layer arithmetic (RMS norms, Q8_K re-quantization, "
+                                        "q/k/v/o/gate/up/down Q4_K dots, SwiGLU, residual adds) on a bounded sample "
+                                        "of the stack; the GPU arm's value is the whole 64-layer stack plus the Q6_K "
+                                        "head per token, in the same unit"},
             "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": nthreads, "kind": "port",
                              "sample": f"{args.ref_layers} stack layers ({wbytes / 1e9:.2f} GB of Q4_K weights) per "
                                        f"step, restated ggml-cpu semantics, {nthreads} threads"},
@@ -611,7 +628,8 @@ def main() -> int:
     ap.add_argument("--per-call", action="store_true", help="one call per projection at every N")
     ap.add_argument("--no-parity", action="store_true", help="skip the N > 1 parity check")
     ap.add_argument("--profile", default=None,
-                    choices=["decode_ffn", "prefill_512", "prefill_q8_0_512", "prefill_q6k_512", "stack", "head"])
+                    choices=["decode_ffn", "verify_ffn", "prefill_512", "prefill_q8_0_512", "prefill_q6k_512", "stack",
+                             "head"])
     ap.add_argument("--source-hash", action="store_true",
                     help="print the hash of the decode GEMV's sources (the source_sha256 of its ncu summary)")
     args = ap.parse_args()

@@ -332,9 +332,9 @@ static bool q8_rows_ok(const GemvArgs &g, int mt) {
            q8r_smem_bytes(int(nb), mr) <= kSmemMax;
 }
 
-template <int MT>
+template <int MT, bool QX = false>
 static cudaError_t launch_q8_rows_t(const Q8RowArgs &a, cudaStream_t st) {
-    auto kern = gemv_q8_0_rows_kernel<MT>;
+    auto kern = gemv_q8_0_rows_kernel<MT, QX>;
     const int dev = current_device();
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     static std::atomic<int> set[kMaxDevices];
@@ -348,7 +348,9 @@ static cudaError_t launch_q8_rows_t(const Q8RowArgs &a, cudaStream_t st) {
     return launch(kern, dim3(unsigned(grid)), dim3(kQ8rWarps * 32), size_t(q8r_smem_bytes(a.nb, MT)), st, a);
 }
 
-static cudaError_t launch_q8_rows(const GemvArgs &g, int mt, cudaStream_t st) {
+// x != NULL: the kernel quantizes the fp32 activations itself (no quantizer launch).
+static cudaError_t launch_q8_rows(const GemvArgs &g, int mt, cudaStream_t st, const float *x = nullptr,
+                                  int64_t x_stride = 0) {
     Q8RowArgs a;
     a.w = g.w[0];
     a.y = g.y[0];
@@ -358,6 +360,9 @@ static cudaError_t launch_q8_rows(const GemvArgs &g, int mt, cudaStream_t st) {
     a.m = mt;
     a.qs = g.act.qs;
     a.d = g.act.d;
+    a.x = x;
+    a.x_stride = x_stride;
+    if (x && mt == 1) return launch_q8_rows_t<1, true>(a, st);
     switch (mt) {
     case 1: return launch_q8_rows_t<1>(a, st);
     case 2: return launch_q8_rows_t<2>(a, st);
@@ -1006,6 +1011,16 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
         return s0.wtype == CPQ_TYPE_Q8_0 ? run_tc<CPQ_TYPE_Q8_0>(a, xp, x_stride, m, wsb, st)
                                          : run_tc<CPQ_TYPE_Q6_K>(a, xp, x_stride, m, wsb, st);
 
+    if (s0.wtype == CPQ_TYPE_Q8_0 && m == 1 && aligned(xp, 16)) {
+        // a single token: the row-pair kernel quantizes it itself (one launch instead of two)
+        GemvArgs g = a;
+        g.act.qs = reinterpret_cast<const int8_t *>(wsb + kWsActOffset);  // alignment checks only
+        g.act.d = reinterpret_cast<const float *>(wsb + kWsActOffset);
+        if (q8_rows_ok(g, 1)) {
+            e = launch_q8_rows(g, 1, st, xp, x_stride);
+            return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "gemv launch");
+        }
+    }
     void *act_ws = wsb + kWsActOffset;
     e = launch_quantize(vt, xp, s0.k, m, x_stride, act_ws, L, nullptr, st);
     if (e != cudaSuccess) return cuda_fail(e, "quantize launch");

@@ -246,6 +246,8 @@ struct Q8RowArgs {
     int m;
     const int8_t *qs;      // Q8_0 quants [m][K]
     const float *d;        // Q8_0 scales [m][nb] (fp16 widened)
+    const float *x;        // or (quantize inside): the fp32 activations [m][x_stride], 16-byte aligned rows
+    int64_t x_stride;
 };
 
 __host__ __device__ constexpr int q8r_stage_bytes(int nb) { return 2 * nb * kQ8_0_Bytes; }
@@ -260,7 +262,56 @@ __host__ __device__ constexpr int q8r_smem_bytes(int nb, int m) {
 }
 __device__ __forceinline__ int q8r_swz(int s) { return s ^ ((s >> 3) & 1); }
 
-template <int MT>
+// Q8_0 quantization of the activations straight into this CTA's shared
+// image, with quantize_q8_0_kernel's arithmetic (x86 AVX2 semantics: d =
+// fp16(amax / 127), q = round-half-even(x * 127 / amax)): four lanes per
+// 32-element block, 8 elements each.
+__device__ __forceinline__ void q8r_quantize_into(const Q8RowArgs &a, int8_t *xq, float *xd) {
+    const int lane = threadIdx.x & 31, sub = lane & 3;
+    const int nb = a.nb;
+    const int tstride = nb * 2;  // 16-byte slots per token row
+    const int total = a.m * nb;
+    for (int base = int(threadIdx.x >> 2) - (lane >> 2); base < total; base += int(blockDim.x >> 2)) {
+        const int blk = base + (lane >> 2);
+        const bool valid = blk < total;
+        const int t = valid ? blk / nb : 0, b = valid ? blk - t * nb : 0;
+        float v[8];
+        if (valid) {
+            const float *xb = a.x + t * a.x_stride + b * kQK8_0 + sub * 8;
+            const float4 v0 = *reinterpret_cast<const float4 *>(xb);
+            const float4 v1 = *reinterpret_cast<const float4 *>(xb + 4);
+            v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
+            v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = 0.0f;
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(v[e]));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        if (!valid) continue;
+        const __half hd = __float2half_rn(__fdiv_rn(amax, 127.0f));
+        const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            int q = __float2int_rn(__fmul_rn(v[e], id));
+            q = q < -128 ? -128 : (q > 127 ? 127 : q);
+            if (e < 4) lo |= (uint32_t(q) & 0xffu) << (8 * e);
+            else hi |= (uint32_t(q) & 0xffu) << (8 * (e - 4));
+        }
+        // bytes 8 sub .. 8 sub + 7 of the block: half (sub & 1) of 16-byte slot 2b + sub / 2
+        uint8_t *slot = reinterpret_cast<uint8_t *>(xq) + 16 * (t * tstride + q8r_swz(2 * b + (sub >> 1)));
+        *reinterpret_cast<uint2 *>(slot + 8 * (sub & 1)) = make_uint2(lo, hi);
+        if (sub == 0) xd[t * nb + b] = __half2float(hd);
+    }
+}
+
+// QX: the activations arrive as fp32 and are quantized here (a.x) instead of
+// by a separate quantizer launch (a.qs, a.d).
+template <int MT, bool QX = false>
 __global__ void __launch_bounds__(kQ8rWarps * 32, 1) gemv_q8_0_rows_kernel(const __grid_constant__ Q8RowArgs a) {
     constexpr int S = q8r_stages(MT);
     extern __shared__ __align__(128) uint8_t smem[];
@@ -299,11 +350,13 @@ __global__ void __launch_bounds__(kQ8rWarps * 32, 1) gemv_q8_0_rows_kernel(const
     for (int s = 0; s < S && p_issue < p_end; s++) issue(s);
 
     pdl_wait();
-    if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(act_bar, d_bytes);
-        bulk_g2s(xd, a.d, d_bytes, act_bar);
-    }
-    {
+    if (QX) {
+        q8r_quantize_into(a, xq, xd);
+    } else {
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(act_bar, d_bytes);
+            bulk_g2s(xd, a.d, d_bytes, act_bar);
+        }
         const int4 *src = reinterpret_cast<const int4 *>(a.qs);
         int4 *dst = reinterpret_cast<int4 *>(xq);
         const int nslots = int(qs_bytes >> 4);
@@ -311,7 +364,7 @@ __global__ void __launch_bounds__(kQ8rWarps * 32, 1) gemv_q8_0_rows_kernel(const
     }
     __syncthreads();
     const int64_t pre = p_issue - p_begin;
-    if (!mbar_wait_bounded(act_bar, 0)) {
+    if (!QX && !mbar_wait_bounded(act_bar, 0)) {
         for (int64_t j = 0; j < pre; j++) mbar_wait_bounded(&bars[j], 0);
         return;
     }
