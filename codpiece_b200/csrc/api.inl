@@ -843,12 +843,41 @@ template <int WT> static void (*tc_kernel())(TcArgs) {
     return WT == CPQ_TYPE_Q4_K ? gemm_q4k_tc_kernel : WT == CPQ_TYPE_Q8_0 ? gemm_q8_0_tc_kernel : gemm_q6k_tc_kernel;
 }
 
+// K ranges per (row pair, token tile) for the tensor-core GEMM, for chunks of
+// at most kTcSplitMaxTokens tokens (one token tile): predicted time = waves of
+// units (row pairs x s, over the SM pairs) times a unit's tensor time
+// (2*256*tile_n*K/s FLOP at about 15.5 TFLOP/s per SM pair), plus, for s > 1,
+// the partial planes and Y through HBM at about 6 TB/s; each range keeps >= 4
+// superblocks. Measured on [5120 x 17408]: M = 64 92.5 -> 44.4 us with 3
+// ranges; at M = 512 and 2048 the partial planes and the per-unit epilogue
+// cost more than the idle SM pairs (114 -> 120 us, 359 -> 446 us), so larger
+// chunks keep one range.
+constexpr int kTcMaxSplits = 4;
+constexpr int64_t kTcSplitMaxTokens = 128;
+static int tc_k_splits(int64_t n, int64_t m, int64_t nbk, int sm_pairs) {
+    if (m > kTcSplitMaxTokens) return 1;
+    const int64_t n_tok = (m + kTcMaxTok - 1) / kTcMaxTok;
+    const int64_t tile_n = int64_t(align_up(size_t((m + n_tok - 1) / n_tok), 32));
+    const int64_t units = ((n + 2 * kTcRows - 1) / (2 * kTcRows)) * n_tok;
+    const double k = double(nbk) * kQK_K;
+    auto cost = [&](int s) {
+        const double unit = 2.0 * 2 * kTcRows * double(tile_n) * k / s / 15.5e12;
+        const double waves = double((units * s + sm_pairs - 1) / sm_pairs);
+        return waves * unit + (s > 1 ? double(s + 1) * double(m) * double(n) * 4.0 / 6.0e12 : 0.0);
+    };
+    int best = 1;
+    for (int s = 2; s <= kTcMaxSplits && nbk / s >= 4; s++)
+        if (cost(s) < cost(best) * 0.97) best = s;
+    return best;
+}
+
 // M > 16 (chunked prefill): X is quantized once (Q8_K for Q4_K / Q6_K, Q8_0 for
 // Q8_0) into fp16 d*q, then each weight runs as one tcgen05 GEMM launch
 // (gemm_tc.cuh) over CTA pairs. Token tiles are as few as possible and
 // balanced (tile_n a multiple of 32, at most 256).
 template <int WT>
-static cpq_status run_tc(const GemvArgs &g, const float *x, int64_t x_stride, int64_t m, uint8_t *ws, cudaStream_t st) {
+static cpq_status run_tc(const GemvArgs &g, const float *x, int64_t x_stride, int64_t m, uint8_t *ws, size_t ws_bytes,
+                         cudaStream_t st) {
     const int64_t k = g.k, nbk = k / kQK_K;
     const int dev = current_device();
     if (dev < 0 || dev >= kMaxDevices) return fail(CPQ_ERR_CUDA, "no current device");
@@ -885,6 +914,9 @@ static cpq_status run_tc(const GemvArgs &g, const float *x, int64_t x_stride, in
     a.nbk = int(nbk);
     a.tile_n = tile_n;
     a.w_rs = int64_t(g.rs);
+    // partial products of K-split launches: after the activation and prologue regions
+    const size_t part_off = kWsActOffset + act_region_bytes(vec_dot_type(WT), k, m) + align_up(size_t(m) * k * 4, 256);
+    const size_t part_room = ws_bytes > part_off ? ws_bytes - part_off : 0;
     for (int i = 0; i < g.n_w; i++) {
         const int64_t n = g.row_start[i + 1] - g.row_start[i];
         if (n == 0) continue;
@@ -904,10 +936,19 @@ static cpq_status run_tc(const GemvArgs &g, const float *x, int64_t x_stride, in
         a.n = n;
         a.n_pairs = int(pairs);
         a.n_tok_tiles = int(n_tok_tiles);
-        // persistent: one CTA pair per two SMs (at most one per tile)
-        const int64_t grid_pairs = std::min<int64_t>(sm_count(dev) / 2, pairs * n_tok_tiles);
+        int splits = tc_k_splits(n, m, nbk, sm_count(dev) / 2);
+        while (splits > 1 && size_t(splits) * size_t(m) * size_t(n) * 4 > part_room) splits--;
+        a.k_splits = splits;
+        a.part = splits > 1 ? reinterpret_cast<float *>(ws + part_off) : nullptr;
+        // persistent: one CTA pair per two SMs (at most one per unit)
+        const int64_t grid_pairs = std::min<int64_t>(sm_count(dev) / 2, pairs * n_tok_tiles * splits);
         e = launch_pair(kern, dim3(unsigned(2 * grid_pairs)), dim3(kTcThreads), size_t(smem), st, a);
         if (e != cudaSuccess) return cuda_fail(e, "tensor-core gemm launch");
+        if (splits > 1) {
+            e = launch(tc_split_reduce_kernel, dim3(unsigned(std::min<int64_t>((m * n + 255) / 256, 148 * 16))),
+                       dim3(256), 0, st, a.part, splits, m, n, a.y, a.y_stride);
+            if (e != cudaSuccess) return cuda_fail(e, "split reduce launch");
+        }
     }
     return CPQ_SUCCESS;
 }
@@ -1005,11 +1046,11 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
         x_stride = s0.k;
     }
     if (s0.wtype == CPQ_TYPE_Q4_K)
-        return m > kMmaMaxTokens ? run_tc<CPQ_TYPE_Q4_K>(a, xp, x_stride, m, wsb, st)
+        return m > kMmaMaxTokens ? run_tc<CPQ_TYPE_Q4_K>(a, xp, x_stride, m, wsb, ws_bytes, st)
                                  : run_q4k_mma(a, xp, x_stride, m, wsb, st);
     if (m > kTcMinTokens && tc_ok(s0.wtype, a))
-        return s0.wtype == CPQ_TYPE_Q8_0 ? run_tc<CPQ_TYPE_Q8_0>(a, xp, x_stride, m, wsb, st)
-                                         : run_tc<CPQ_TYPE_Q6_K>(a, xp, x_stride, m, wsb, st);
+        return s0.wtype == CPQ_TYPE_Q8_0 ? run_tc<CPQ_TYPE_Q8_0>(a, xp, x_stride, m, wsb, ws_bytes, st)
+                                         : run_tc<CPQ_TYPE_Q6_K>(a, xp, x_stride, m, wsb, ws_bytes, st);
 
     if (s0.wtype == CPQ_TYPE_Q8_0 && m == 1 && aligned(xp, 16)) {
         // a single token: the row-pair kernel quantizes it itself (one launch instead of two)
@@ -1137,7 +1178,14 @@ size_t cpq_mul_mat_workspace_size(const cpq_tensor *w, const cpq_tensor *x) {
     if (!w || !x) return 0;
     const int32_t vt = vec_dot_type(w->type);
     if (vt < 0 || x->ne[1] < 0 || w->ne[0] <= 0) return 0;
-    return ws_need(vt, w->ne[0], std::max<int64_t>(x->ne[1], 1));
+    const int64_t m = std::max<int64_t>(x->ne[1], 1), k = w->ne[0], n = std::max<int64_t>(w->ne[1], 1);
+    size_t need = ws_need(vt, k, m);
+    if (m > kTcMinTokens && k % kQK_K == 0) {  // room for the tensor-core GEMM's K-split partials
+        const int dev = current_device();
+        const int splits = dev >= 0 ? tc_k_splits(n, m, k / kQK_K, sm_count(dev) / 2) : 1;
+        if (splits > 1) need += size_t(splits) * size_t(m) * size_t(n) * 4;
+    }
+    return need;
 }
 
 cpq_status cpq_mul_mat_ws(const cpq_tensor *w, const cpq_tensor *x, cpq_tensor *y, void *workspace,

@@ -145,6 +145,8 @@ struct alignas(64) TcArgs {
     int tile_n;          // tokens per pair tile (multiple of 32, 32..256)
     int n_pairs;         // 256-row tiles (row pairs)
     int n_tok_tiles;     // token tiles
+    int k_splits;        // K ranges per (row pair, token tile); > 1: fp32 partials to part
+    float *part;         // [k_splits][m][n] partial products (k_splits > 1)
 };
 
 // ---- tcgen05 / descriptor helpers ------------------------------------------
@@ -421,12 +423,18 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
     const int tile_n = a.tile_n, half_n = tile_n / 2;
-    const int nk = a.nbk * (kQK_K / kTcK);        // stages per tile
-    const int64_t n_tiles = int64_t(a.n_pairs) * a.n_tok_tiles;
+    // a work unit ("tile") is a row pair x token tile x K range (superblocks [kb0, kb1))
+    const int ks_n = a.k_splits;
+    const int64_t n_tiles = int64_t(a.n_pairs) * a.n_tok_tiles * ks_n;
+    auto tile_kb0 = [&](int64_t tile) { return int(int64_t(tile % ks_n) * a.nbk / ks_n); };
+    auto tile_kb1 = [&](int64_t tile) { return int(int64_t(tile % ks_n + 1) * a.nbk / ks_n); };
+    auto tile_nk = [&](int64_t tile) { return (tile_kb1(tile) - tile_kb0(tile)) * (kQK_K / kTcK); };  // stages
     const int64_t pair = blockIdx.x >> 1, n_pairs_grid = gridDim.x >> 1;
     // this pair's i-th tile: row pair and token tile
-    auto tile_rows = [&](int64_t tile) { return (tile / a.n_tok_tiles) * (2 * kTcRows) + int64_t(rank) * kTcRows; };
-    auto tile_tok = [&](int64_t tile) { return (tile % a.n_tok_tiles) * tile_n; };
+    auto tile_rows = [&](int64_t tile) {
+        return (tile / ks_n / a.n_tok_tiles) * (2 * kTcRows) + int64_t(rank) * kTcRows;
+    };
+    auto tile_tok = [&](int64_t tile) { return (tile / ks_n % a.n_tok_tiles) * tile_n; };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcAStages; s++) {
@@ -473,6 +481,7 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
                 // the epilogue has drained the previous tile's accumulator
                 if (it > 0 && !tc_wait(acc_empty, uint32_t(it - 1) & 1u, abort_flag)) break;
                 tc_fence_after();
+                const int nk = tile_nk(tile);
                 for (int t = 0; t < nk; t++, g++) {
                     const int sa = int(g % kTcAStages), sb = int(g % kTcBStages);
                     if (!tc_wait(&fullA[sa], uint32_t(g / kTcAStages) & 1u, abort_flag) ||
@@ -511,6 +520,7 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
             bool ok = true;
             for (int64_t tile = pair; tile < n_tiles && ok; tile += n_pairs_grid) {
                 const int tok = int(tile_tok(tile)) + int(rank) * half_n;
+                const int nk = tile_nk(tile), k0 = tile_kb0(tile) * (kQK_K / kTcK);
                 for (int t = 0; t < nk; t++, g++) {
                     const int s = int(g % kTcBStages);
                     const uint32_t ph = uint32_t(g / kTcBStages) & 1u;
@@ -522,8 +532,8 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
                     const uint32_t bar0 = cluster_addr(&fullB[s], 0);
 #pragma unroll
                     for (int q = 0; q < kTcK / kTcAtomK; q++)
-                        tma_load_2d_pair(sB + s * kTcBBytes + q * kTcBAtomBytes, &a.tmap_x, t * kTcK + q * kTcAtomK,
-                                         tok, bar0);
+                        tma_load_2d_pair(sB + s * kTcBBytes + q * kTcBAtomBytes, &a.tmap_x,
+                                         (k0 + t) * kTcK + q * kTcAtomK, tok, bar0);
                 }
             }
             // no copy may land after the CTAs have exited: rank 0 waits for the last stages issued
@@ -539,7 +549,7 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
         bool ok = true;
         for (int64_t tile = pair; tile < n_tiles && ok; tile += n_pairs_grid) {
             const int64_t row0 = tile_rows(tile);
-            for (int kb = 0; kb < a.nbk; kb++, g++) {
+            for (int kb = tile_kb0(tile); kb < tile_kb1(tile); kb++, g++) {
                 const int s = int(g % kSlots);
                 const uint32_t ph = uint32_t(g / kSlots) & 1u;
                 int good = 0;
@@ -671,16 +681,19 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
             const int64_t tok0 = tile_tok(tile);
             const int64_t orow = tile_rows(tile) + row_of_lane;
             const int64_t tend = a.m < tok0 + tile_n ? a.m : tok0 + tile_n;
+            // a K range's partial products go to its own plane of part; a whole K to Y
+            float *yb = ks_n > 1 ? a.part + (tile % ks_n) * a.m * a.n : a.y;
+            const int64_t ys = ks_n > 1 ? a.n : a.y_stride;
             const int half = (((tile_n + 1) / 2) + 31) & ~31;
             const int cbeg = grp * half, cend = grp ? tile_n : (half < tile_n ? half : tile_n);
             for (int c0 = cbeg; c0 < cend && tok0 + c0 < tend; c0 += 32) {
                 float v[32];
                 tmem_ld32(tmem + lane_base + uint32_t(c0), v);
                 if (orow < a.n) {
-                    float *yp = a.y + (tok0 + c0) * a.y_stride + orow;
+                    float *yp = yb + (tok0 + c0) * ys + orow;
 #pragma unroll
                     for (int i = 0; i < 32; i++)
-                        if (tok0 + c0 + i < tend) yp[int64_t(i) * a.y_stride] = v[i];
+                        if (tok0 + c0 + i < tend) yp[int64_t(i) * ys] = v[i];
                 }
             }
             tc_fence_before();  // the TMEM reads are complete (tmem_ld32 waits for them)
@@ -698,11 +711,13 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
             int t = grp;
             const int prefill = kTcAStages;  // stages of this tile (both groups) before the epilogue
             const int64_t row0 = tile_rows(tile);
-            for (; t < nk && t < prefill && ok; t += 2) ok = dequant_stage(g0 + t, r0 + (t >> 1), t >> 1, row0);
+            const int nk = tile_nk(tile), kb0 = tile_kb0(tile);
+            for (; t < nk && t < prefill && ok; t += 2)
+                ok = dequant_stage(g0 + t, r0 + (t >> 1), kb0 + (t >> 1), row0);
             if (ok && prev_tile >= 0) ok = epilogue(prev_tile, it - 1);
-            for (; t < nk && ok; t += 2) ok = dequant_stage(g0 + t, r0 + (t >> 1), t >> 1, row0);
+            for (; t < nk && ok; t += 2) ok = dequant_stage(g0 + t, r0 + (t >> 1), kb0 + (t >> 1), row0);
             gs += nk;
-            gr += a.nbk;
+            gr += tile_kb1(tile) - kb0;
             prev_tile = tile;
         }
         if (ok && prev_tile >= 0) epilogue(prev_tile, it - 1);
@@ -724,6 +739,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_q8_0_tc_kernel(const __gri
 }
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_q6k_tc_kernel(const __grid_constant__ TcArgs a) {
     gemm_tc_body<CPQ_TYPE_Q6_K>(a);
+}
+
+// Y = the K ranges' partial products added in range order (deterministic).
+// No early trigger of dependents: the next GEMM may overwrite part only after
+// this kernel has finished reading it.
+__global__ void __launch_bounds__(256) tc_split_reduce_kernel(const float *__restrict__ part, int splits, int64_t m,
+                                                              int64_t n, float *__restrict__ y, int64_t y_stride) {
+    pdl_wait();
+    const int64_t plane = m * n;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < plane; i += int64_t(gridDim.x) * blockDim.x) {
+        float v = part[i];
+        for (int s = 1; s < splits; s++) v = __fadd_rn(v, part[s * plane + i]);
+        const int64_t t = i / n;
+        y[t * y_stride + (i - t * n)] = v;
+    }
 }
 
 // The tensor-core path's activations: each 256-block of x quantized to Q8_K

@@ -146,9 +146,12 @@ def test_prefill_q8_0_q6_k_edge_activations(cuda, oracle, qt):
 
 
 @pytest.mark.parametrize("qt,n,k,m", [(synth.Q8_0, 5120, 5120, 512), (synth.Q8_0, 17408, 5120, 512),
-                                      (synth.Q6_K, 151936, 5120, 512), (synth.Q6_K, 5120, 17408, 300)])
+                                      (synth.Q6_K, 151936, 5120, 512), (synth.Q6_K, 5120, 17408, 300),
+                                      # 64-token chunks: K split into ranges whose partials are added in order
+                                      (synth.Q4_K, 5120, 17408, 64), (synth.Q8_0, 5120, 17408, 64),
+                                      (synth.Q6_K, 5120, 5120, 64)])
 def test_prefill_q8_0_q6_k_full_shapes(cuda, oracle, qt, n, k, m):
-    """The Q8_0 trunk shapes and the Q6_K head at a 512-token chunk: oracle on row slices,
+    """The Q8_0 trunk shapes and the Q6_K head at a 512-token chunk, and K-split 64-token chunks: oracle on row slices,
     every row for the first and last 16 tokens against the M <= 16 integer path."""
     mm = _mm()
     w = mm.synth_weights(qt, k, n, seed=n ^ k ^ m ^ qt)
