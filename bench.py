@@ -19,7 +19,8 @@ Its FFN projections are exactly BASELINE config 2's Q4_K mat-vec shapes,
              inputs resident in HBM); bytes each rank streams (the mirrored
              head on every rank) are config.weight_bytes_per_rank
   tp_parity  N > 1: a 2-layer stack decoded (M = 1, trunk) and verified
-             (M = 8, NCCL) on all ranks against the same stack on one GPU
+             (M = 8, per-call MMA GEMVs), both through the fused NVLink
+             all-reduce, on all ranks against the same stack on one GPU
              before timing; the run fails if either differs by more than 1e-3
   e2e        the same through the public API with host buffers: hidden state
              uploaded from pinned memory and the greedy token read back
@@ -35,7 +36,8 @@ Its FFN projections are exactly BASELINE config 2's Q4_K mat-vec shapes,
              mul_mat (activation pre-pass included) against
              MEASURED_PEAKS.json bf16_tflops
   verify     the same 64-layer stack stepping M = 8 tokens (the speculative
-             verify batch of configs[4]) on all N GPUs (NCCL all-reduce)
+             verify batch of configs[4]) on all N GPUs (fused NVLink all-reduce;
+             --nccl: NCCL)
   small_configs  configs[0] (Q8_0 [5120 x 5120] mat-vec, M = 1) and configs[2]
              (one layer's q/k/v/o and the Q6_K head at M = 2, 4, 8, 16):
              weight GB/s of each mul_mat on rotating weights larger than L2
@@ -409,10 +411,12 @@ def model_bytes(tp, layers: int, head: bool = True) -> int:
     return layers * per_layer + (hp.n_vocab * e // 256 * 210 if head else 0)
 
 
-def verify_step(torch, st, tp, layers: int, rank: int, world: int, comm, barrier, m: int = 8, steps: int = 10):
+def verify_step(torch, st, tp, layers: int, rank: int, world: int, comm, barrier, m: int = 8, steps: int = 10,
+                exchange=None):
     """configs[4]'s verify step: the same stack at M = 8 tokens on all ranks (MMA GEMVs; at N > 1 the
-    row-parallel partial sums go through NCCL). Max over ranks of the device time."""
-    stack = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=0)
+    row-parallel partial sums go through the fused NVLink all-reduce when exchange is given, else NCCL).
+    Max over ranks of the device time."""
+    stack = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=0, ar_exchange=exchange)
     stack.h.copy_(torch.randn(m, 5120, generator=torch.Generator().manual_seed(5)).cuda())
     stack.capture()
     for _ in range(3):
@@ -431,15 +435,15 @@ def verify_step(torch, st, tp, layers: int, rank: int, world: int, comm, barrier
 
 
 def tp_parity(torch, st, tp, comm, exchange, rank: int, world: int, layers: int = 2):
-    """N > 1: a few full-width layers decoded through the trunk (M = 1, fused NVLink all-reduce) and
-    verified (M = 8, NCCL) on all ranks, against the same stack on rank 0's GPU alone (the per-call path,
-    itself checked against the CPU oracle by the tests). Returns rank 0's verdict."""
+    """N > 1: a few full-width layers decoded through the trunk (M = 1) and verified (M = 8, per-call MMA
+    GEMVs), both with the fused NVLink all-reduce, on all ranks, against the same stack on rank 0's GPU
+    alone (the per-call path, itself checked against the CPU oracle by the tests). Returns rank 0's verdict."""
     import torch.distributed as dist
     out = {}
     for m, trunk in ((1, True), (8, False)):
         h0 = torch.randn(m, 5120, generator=torch.Generator().manual_seed(11 + m)) * 2
-        s = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=5,
-                     ar_exchange=exchange if trunk else None, use_trunk=trunk)
+        s = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=5, ar_exchange=exchange,
+                     use_trunk=trunk)
         s.h.copy_(h0)
         s.step_body()
         torch.cuda.synchronize()
@@ -454,7 +458,7 @@ def tp_parity(torch, st, tp, comm, exchange, rank: int, world: int, layers: int 
             ref.step_body()
             torch.cuda.synchronize()
             lr, hr = ref.logits.cpu(), ref.h_final.cpu()
-            key = "decode_m1_trunk" if trunk else "verify_m8_nccl"
+            key = "decode_m1_trunk" if trunk else "verify_m8_fused_ar"
             out[key] = {"h_rel": float((h_tp - hr).abs().max() / hr.abs().max()),
                         "logits_rel": float((logits_tp - lr).abs().max() / lr.abs().max()),
                         "tok_match": tok_tp.tolist() == ref.tok.cpu().tolist(),
@@ -783,14 +787,16 @@ def main() -> int:
     del stack
     torch.cuda.empty_cache()
     if not args.no_verify:
-        vms = verify_step(torch, st, tp, args.layers, rank, world, comm, barrier)
+        vms = verify_step(torch, st, tp, args.layers, rank, world, comm, barrier,
+                          exchange=exchange if (world > 1 and not args.nccl) else None)
         tv = torch.tensor([vms], dtype=torch.float64, device="cuda")
         if world > 1:
             dist.all_reduce(tv, op=dist.ReduceOp.MAX)
         vms = float(tv[0])
         verify = {"m": 8, "ms_per_step": round(vms, 4), "tok_per_s": round(8e3 / vms, 1),
                   "model_GBs": round(total_bytes / vms / 1e6, 1), "layers": args.layers,
-                  "tp_allreduce": "none" if world == 1 else "nccl"}
+                  "tp_allreduce": "none" if world == 1 else "nccl" if args.nccl else
+                  "fused into the MMA GEMV over NVLink peer memory"}
     barrier()
     if comm is not None:
         comm.destroy()

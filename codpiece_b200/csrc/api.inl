@@ -675,11 +675,13 @@ static size_t act_region_bytes(int32_t vt, int64_t k, int64_t m) {
 }
 
 // up != NULL: the input is silu(x) * up, formed inside the quantizer (x = gate rows).
+// ar_out: weight 0's outputs go to every rank through the fused all-reduce channel.
 static cpq_status run_q4k_mma(const GemvArgs &g, const float *x, int64_t x_stride, int64_t m, uint8_t *ws,
-                              cudaStream_t st, const float *up = nullptr) {
+                              cudaStream_t st, const float *up = nullptr, const ArOut *ar_out = nullptr) {
     const int64_t k = g.k, nbk = k / kQK_K;
     static thread_local MmaArgs a;  // large (tensor maps); filled per call
     std::memset(&a, 0, sizeof a);
+    if (ar_out) a.ar = *ar_out;
     a.n_w = g.n_w;
     a.mb_start[0] = 0;
     for (int i = 0; i < g.n_w; i++) {
@@ -1004,33 +1006,58 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
     int64_t x_stride = int64_t(x->nb[1] / 4);
 
     cudaError_t e;
+    ArOut mma_ar;  // verify (M = 4..16) with a fused all-reduce output
+    const ArOut *mma_ar_p = nullptr;
     if (r_ar || y_ar) {
-        // the fused allreduce lives in the decode GEMV (row kernel + its act_prep)
-        if (!(s0.wtype == CPQ_TYPE_Q4_K && m <= kRowMaxTokens && row_smem_bytes(s0.k, int(m)) <= kSmemMax))
-            return fail(CPQ_ERR_UNSUPPORTED, "fused allreduce: Q4_K with M <= %d only", kRowMaxTokens);
         const char *why = "";
-        ArIn ain;
-        ArOut aout;
+        const bool row_path = s0.wtype == CPQ_TYPE_Q4_K && m <= kRowMaxTokens && row_smem_bytes(s0.k, int(m)) <= kSmemMax;
+        const bool mma_path = s0.wtype == CPQ_TYPE_Q4_K && m > kRowMaxTokens && m <= kMmaMaxTokens;
+        if (!row_path && !mma_path)
+            return fail(CPQ_ERR_UNSUPPORTED, "fused allreduce: Q4_K with M <= %d only", kMmaMaxTokens);
         if (r_ar) {
             if (pro.mode != CPQ_PRO_RMS || pro.r)
                 return fail(CPQ_ERR_INVALID_ARG, "fused allreduce input: the prologue must be RMS with r = NULL");
             if (!ar_ready(r_ar, m * s0.k, &why)) return fail(CPQ_ERR_INVALID_ARG, "fused allreduce input: %s", why);
-            ain = ar_in_of(r_ar, s0.k);
         }
         if (y_ar) {
             if (n_w != 1) return fail(CPQ_ERR_INVALID_ARG, "fused allreduce output: one weight per call");
             if (!ar_ready(y_ar, m * a.row_start[1], &why))
                 return fail(CPQ_ERR_INVALID_ARG, "fused allreduce output: %s", why);
-            aout = ar_out_of(y_ar, a.row_start[1]);
         }
-        return run_q4k_row(a, xp, x_stride, int(m), pro, wsb, st, r_ar ? &ain : nullptr, y_ar ? &aout : nullptr);
+        if (row_path) {
+            // decode: the all-reduce lives in the row GEMV and its act_prep
+            ArIn ain;
+            ArOut aout;
+            if (r_ar) ain = ar_in_of(r_ar, s0.k);
+            if (y_ar) aout = ar_out_of(y_ar, a.row_start[1]);
+            return run_q4k_row(a, xp, x_stride, int(m), pro, wsb, st, r_ar ? &ain : nullptr, y_ar ? &aout : nullptr);
+        }
+        // verify: the input's all-reduce is added to x first (h_out, or a workspace row block),
+        // then the RMS prologue and the MMA GEMV run as without it; the output's goes out of the GEMV
+        if (r_ar) {
+            if (x_stride != s0.k || s0.k % 8)
+                return fail(CPQ_ERR_UNSUPPORTED, "fused allreduce input at M > %d: dense rows, K %% 8 = 0", kRowMaxTokens);
+            float *hsum = pro.h_out ? pro.h_out
+                                    : reinterpret_cast<float *>(wsb + kWsActOffset + act_region_bytes(vt, s0.k, m));
+            ArIn in = ar_in_of(r_ar, s0.k);
+            const dim3 grid(unsigned((s0.k + 2047) / 2048), unsigned(m));
+            in.n_ctas = grid.x * grid.y;
+            e = launch(ar_add_kernel, grid, dim3(256), 0, st, in, xp, hsum, s0.k);
+            if (e != cudaSuccess) return cuda_fail(e, "all-reduce add launch");
+            xp = hsum;
+            pro.h_out = nullptr;
+        }
+        if (y_ar) {
+            mma_ar = ar_out_of(y_ar, a.row_start[1]);
+            mma_ar_p = &mma_ar;
+        }
     }
     if (s0.wtype == CPQ_TYPE_Q4_K && m <= kRowMaxTokens && row_smem_bytes(s0.k, int(m)) <= kSmemMax)
         return run_q4k_row(a, xp, x_stride, int(m), pro, wsb, st);
 
     if (pro.mode == CPQ_PRO_SWIGLU && s0.wtype == CPQ_TYPE_Q4_K && m <= kMmaMaxTokens && aligned(xp, 16) &&
         x_stride % 4 == 0)
-        return run_q4k_mma(a, xp, x_stride, m, wsb, st, pro.r);  // SwiGLU inside the quantizer
+        return run_q4k_mma(a, xp, x_stride, m, wsb, st, pro.r, mma_ar_p);  // SwiGLU inside the quantizer
     if (pro.mode != CPQ_PRO_NONE) {
         // the other paths quantize an fp32 input: apply the prologue into the workspace first
         float *tmp = reinterpret_cast<float *>(wsb + kWsActOffset + act_region_bytes(vt, s0.k, m));
@@ -1047,7 +1074,7 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
     }
     if (s0.wtype == CPQ_TYPE_Q4_K)
         return m > kMmaMaxTokens ? run_tc<CPQ_TYPE_Q4_K>(a, xp, x_stride, m, wsb, ws_bytes, st)
-                                 : run_q4k_mma(a, xp, x_stride, m, wsb, st);
+                                 : run_q4k_mma(a, xp, x_stride, m, wsb, st, nullptr, mma_ar_p);
     if (m > kTcMinTokens && tc_ok(s0.wtype, a))
         return s0.wtype == CPQ_TYPE_Q8_0 ? run_tc<CPQ_TYPE_Q8_0>(a, xp, x_stride, m, wsb, ws_bytes, st)
                                          : run_tc<CPQ_TYPE_Q6_K>(a, xp, x_stride, m, wsb, ws_bytes, st);

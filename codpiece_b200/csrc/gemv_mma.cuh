@@ -91,6 +91,7 @@ struct alignas(64) MmaArgs {
     int act_smem;            // > 0: bytes of the activation image, copied into shared memory after the ring
     float *partials;         // [warp][2 segments][16 rows][16 tokens]
     int *counters;           // [row block], zero between calls
+    ArOut ar;                // on: weight 0's rows go as LL words to every rank (the fused all-reduce)
 };
 
 __device__ __forceinline__ void mma_s8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -301,6 +302,19 @@ __global__ void __launch_bounds__(W * 32) gemv_q4k_mma_kernel(const __grid_const
 
     pdl_wait();
     pdl_launch_dependents();
+    // the all-reduce's sequence number (advanced by the consumer of the previous one)
+    const unsigned ar_e = a.ar.on ? *reinterpret_cast<const volatile unsigned *>(a.ar.seq) + 1u : 0u;
+    // a finished output: to Y, or (fused all-reduce) as an LL word (ar_e << 32 | value) into
+    // slot (ar_e % kArSlots, this rank) of every rank's receive buffer
+    auto out_row = [&](int wi, int t, int64_t row, float v) {
+        if (!a.ar.on) {
+            a.y[wi][size_t(t) * a.y_stride[wi] + row] = v;
+            return;
+        }
+        const int64_t off = (int64_t(ar_e % kArSlots) * a.ar.world + a.ar.rank) * a.ar.n_max + int64_t(t) * a.ar.n + row;
+        const uint64_t w = (uint64_t(ar_e) << 32) | __float_as_uint(v);
+        for (int d = 0; d < a.ar.world; d++) st_relaxed_sys_u64(a.ar.peer[d] + off, w);
+    };
     ActFrag act = a.act;
     if (SM) {
         // the activation image (quants, split 32-sums, scales) into shared memory after the ring
@@ -389,7 +403,7 @@ __global__ void __launch_bounds__(W * 32) gemv_q4k_mma_kernel(const __grid_const
                     for (int i = 0; i < 4; i++) {
                         const int t = ng * 8 + 2 * tig + (i & 1);
                         const int r = gid + 8 * (i >> 1);
-                        if (t < a.m && r < rows_here) a.y[wi][size_t(t) * a.y_stride[wi] + row0 + r] = acc[ng][i];
+                        if (t < a.m && r < rows_here) out_row(wi, t, row0 + r, acc[ng][i]);
                     }
             } else {
                 const int64_t first = owner_warp(c_mb * nbk, G, T);
@@ -457,7 +471,7 @@ __global__ void __launch_bounds__(W * 32) gemv_q4k_mma_kernel(const __grid_const
                         for (int i = 0; i < 4; i++) {
                             const int t = ng * 8 + 2 * tig + (i & 1);
                             const int r = gid + 8 * (i >> 1);
-                            if (t < a.m && r < rows_here) a.y[wi][size_t(t) * a.y_stride[wi] + row0 + r] = sum[ng][i];
+                            if (t < a.m && r < rows_here) out_row(wi, t, row0 + r, sum[ng][i]);
                         }
                     if (lane == 0) a.counters[c_mb] = 0;  // ready for the next call
                 }

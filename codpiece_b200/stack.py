@@ -134,7 +134,7 @@ class Stack:
         # Row-parallel partial sums: through the fused NVLink allreduce when the
         # caller supplies a handle exchange (decode M <= 3 with the head), else NCCL.
         self.ar: mm.ArChannel | None = None
-        if ar_exchange is not None and world > 1 and m <= 3 and head:
+        if ar_exchange is not None and world > 1 and m <= 16 and head:
             self.ar = mm.ArChannel(world, rank, m * e, self.dev.index)
             self.ar.connect(list(ar_exchange(self.ar.ipc_handle)))
         if use_plan:

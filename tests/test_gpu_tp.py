@@ -33,8 +33,10 @@ def _ngpus():
 
 
 @pytest.mark.parametrize("world,layers,m,mode", [(2, 2, 1, "nccl"), (2, 2, 8, "nccl"), (2, 3, 1, "ar"), (2, 2, 3, "ar"),
+                                                 (2, 3, 8, "ar"), (2, 2, 13, "ar"),
                                                  (2, 3, 1, "trunk"), (4, 2, 1, "ar"), (4, 3, 1, "trunk"),
-                                                 (8, 2, 1, "ar"), (8, 3, 1, "trunk"), (8, 2, 8, "nccl")])
+                                                 (4, 2, 8, "ar"), (8, 2, 1, "ar"), (8, 3, 1, "trunk"),
+                                                 (8, 2, 8, "nccl"), (8, 3, 8, "ar")])
 def test_tensor_parallel_stack_matches_tp1(cuda, tmp_path, world, layers, m, mode):
     """mode "ar": the row-parallel partial sums go through the fused NVLink allreduce
     (cpq_mul_mat_fused_ar); "nccl": through cpq_tp_allreduce_f32; "trunk": the
