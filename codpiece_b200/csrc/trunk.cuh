@@ -19,7 +19,9 @@
 //    ever waits for the TMA unit to accept a copy.
 //  * Work split inside a phase: the CTA-range split of the decode GEMV
 //    (gemv_row.cuh), with its in-CTA combination of row-block parts and the
-//    tail-cut hand-off to the next CTA.
+//    tail-cut hand-off to the next CTA; or, for phases with few row blocks
+//    per CTA (the small shards of tensor parallelism), ranges of whole row
+//    blocks, which no CTA waits on another for.
 //  * Hand-offs between phases. Every CTA that produced outputs of phase p
 //    adds one to phase p's counter; a CTA that reads them waits (one thread,
 //    short back-off) until the counter holds all of the phase's CTAs, then
@@ -109,7 +111,7 @@ struct TrPhase {
     int write_h;      // this phase's publication of R also stores it to the run's h_out
     const float *g;   // RMS weight (or null)
     float eps;
-    int pad;
+    int whole;        // CTA ranges hold whole row blocks (no block cut between two CTAs)
     float *y_plain[kTrMaxW];        // kTrOutVec: plain fp32 outputs of weights 1, 2 (k, v)
     int64_t n[kTrMaxW];             // rows per weight (pairs: gate rows)
     int64_t mb_start[kTrMaxW + 1];  // prefix sums of row blocks per weight; mb_start[n_w] = total
@@ -193,9 +195,14 @@ __device__ __forceinline__ bool tr_range(const TrPhase *P, int64_t c, TrRange &r
     const int64_t C = P->ctas;
     if (n_w == 0 || c >= C) return false;
     const int nbk = P->nbk;
-    const int64_t T = P->mb_start[n_w] * nbk;
-    r.lo = c * T / C;
-    r.hi = (c + 1) * T / C;
+    const int64_t RB = P->mb_start[n_w], T = RB * nbk;
+    if (P->whole) {
+        r.lo = (c * RB / C) * nbk;
+        r.hi = ((c + 1) * RB / C) * nbk;
+    } else {
+        r.lo = c * T / C;
+        r.hi = (c + 1) * T / C;
+    }
     r.L = r.hi - r.lo;
     r.b0 = (r.hi % nbk) ? (r.hi - r.hi % nbk > r.lo ? r.hi - r.hi % nbk : r.lo) : r.hi;
     r.LB = r.hi - r.b0;

@@ -130,7 +130,17 @@ extern "C" cpq_status cpq_trunk_create(const cpq_trunk_layer *layers, int n_laye
         r_pub = P.in_pub;
     };
     auto finish = [&](TrPhase &P) {  // row blocks -> CTAs with work; the counter of the phase's input
-        if (P.n_w > 0) P.ctas = int(std::min<int64_t>(grid, P.mb_start[P.n_w]));
+        if (P.n_w > 0) {
+            const int64_t rb = P.mb_start[P.n_w];
+            P.ctas = int(std::min<int64_t>(grid, rb));
+            // whole row blocks per CTA when that costs a warp no more stages than the balanced
+            // split, or one more when phases are a few stages per warp (the small shards of tensor
+            // parallelism: there the balanced split's block cuts, which make CTAs wait on their
+            // neighbours' words, cost more than a stage; TP8-shaped trunk 34.1 -> 31.3 us/layer)
+            const int64_t whole_stages = ((rb + P.ctas - 1) / P.ctas * P.nbk + kTrWarps - 1) / kTrWarps;
+            const int64_t range_stages = (rb * P.nbk + int64_t(P.ctas) * kTrWarps - 1) / (int64_t(P.ctas) * kTrWarps);
+            P.whole = whole_stages <= range_stages || (range_stages <= 4 && whole_stages <= range_stages + 1);
+        }
         const int idx = int(ph.size());
         if (P.n_fold > 0) {
             r_cnt = 1 + 2 * idx;
