@@ -3,21 +3,24 @@
 
 Workload (every N): the 27B-shaped stack of BASELINE config 5 --
 64 layers of Q4_K q/k/v/o/gate/up/down (hidden 5120, q 6144, kv 1024,
-FFN 17408) plus a mirrored Q6_K head over vocab 151936 -- decoding M = 1
+FFN 17408) plus a Q6_K head over vocab 151936 -- decoding M = 1
 token per step, tensor-parallel over N GPUs (one process per GPU). Each
 projection is one fused call (activation image + decode GEMV) and the
 row-parallel partial sums cross NVLink inside the GEMV (--nccl: through NCCL);
 From 4 ranks on (or with --trunk) each rank's 64 layers run as one
 persistent kernel instead (cpq_trunk_run, the all-reduce inside it);
 --per-call keeps one call per projection at every N. The head is a fused Q6_K mul_mat
-plus argmax.
+plus argmax; at N > 1 its rows (the vocabulary) are split over the ranks
+(split.rs's optional N split) and the greedy token is found across them
+through the NVLink channel (--mirrored-head: the whole head on every rank,
+split.rs's default).
 Its FFN projections are exactly BASELINE config 2's Q4_K mat-vec shapes,
 64 times over.
 
   value      model GB/s = the unsharded model's weight bytes (12.906 GB, the
              head counted once) / max-over-ranks ms per token (CUDA events,
-             inputs resident in HBM); bytes each rank streams (the mirrored
-             head on every rank) are config.weight_bytes_per_rank
+             inputs resident in HBM); bytes each rank streams are
+             config.weight_bytes_per_rank
   tp_parity  N > 1: a 2-layer stack decoded (M = 1, trunk) and verified
              (M = 8, per-call MMA GEMVs), both through the fused NVLink
              all-reduce, on all ranks against the same stack on one GPU
@@ -412,11 +415,11 @@ def model_bytes(tp, layers: int, head: bool = True) -> int:
 
 
 def verify_step(torch, st, tp, layers: int, rank: int, world: int, comm, barrier, m: int = 8, steps: int = 10,
-                exchange=None):
+                exchange=None, hp=None):
     """configs[4]'s verify step: the same stack at M = 8 tokens on all ranks (MMA GEMVs; at N > 1 the
     row-parallel partial sums go through the fused NVLink all-reduce when exchange is given, else NCCL).
     Max over ranks of the device time."""
-    stack = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=0, ar_exchange=exchange)
+    stack = st.Stack(hp or tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=0, ar_exchange=exchange)
     stack.h.copy_(torch.randn(m, 5120, generator=torch.Generator().manual_seed(5)).cuda())
     stack.capture()
     for _ in range(3):
@@ -434,7 +437,7 @@ def verify_step(torch, st, tp, layers: int, rank: int, world: int, comm, barrier
     return ms
 
 
-def tp_parity(torch, st, tp, comm, exchange, rank: int, world: int, layers: int = 2):
+def tp_parity(torch, st, tp, comm, exchange, rank: int, world: int, layers: int = 2, hp=None):
     """N > 1: a few full-width layers decoded through the trunk (M = 1) and verified (M = 8, per-call MMA
     GEMVs), both with the fused NVLink all-reduce, on all ranks, against the same stack on rank 0's GPU
     alone (the per-call path, itself checked against the CPU oracle by the tests). Returns rank 0's verdict."""
@@ -442,7 +445,7 @@ def tp_parity(torch, st, tp, comm, exchange, rank: int, world: int, layers: int 
     out = {}
     for m, trunk in ((1, True), (8, False)):
         h0 = torch.randn(m, 5120, generator=torch.Generator().manual_seed(11 + m)) * 2
-        s = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=5, ar_exchange=exchange,
+        s = st.Stack(hp or tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=5, ar_exchange=exchange,
                      use_trunk=trunk)
         s.h.copy_(h0)
         s.step_body()
@@ -457,7 +460,8 @@ def tp_parity(torch, st, tp, comm, exchange, rank: int, world: int, layers: int 
             ref.h.copy_(h0)
             ref.step_body()
             torch.cuda.synchronize()
-            lr, hr = ref.logits.cpu(), ref.h_final.cpu()
+            hr = ref.h_final.cpu()
+            lr = ref.logits.cpu()[:, :logits_tp.shape[1]]  # rank 0's rows of a split head (all when mirrored)
             key = "decode_m1_trunk" if trunk else "verify_m8_fused_ar"
             out[key] = {"h_rel": float((h_tp - hr).abs().max() / hr.abs().max()),
                         "logits_rel": float((logits_tp - lr).abs().max() / lr.abs().max()),
@@ -630,6 +634,7 @@ def main() -> int:
     ap.add_argument("--nccl", action="store_true", help="TP partial sums through NCCL (not with --trunk)")
     ap.add_argument("--trunk", action="store_true", help="the persistent trunk kernel at every N")
     ap.add_argument("--per-call", action="store_true", help="one call per projection at every N")
+    ap.add_argument("--mirrored-head", action="store_true", help="the LM head on every rank (no vocabulary split)")
     ap.add_argument("--no-parity", action="store_true", help="skip the N > 1 parity check")
     ap.add_argument("--profile", default=None,
                     choices=["decode_ffn", "verify_ffn", "prefill_512", "prefill_q8_0_512", "prefill_q6k_512", "stack",
@@ -687,9 +692,14 @@ def main() -> int:
         if world > 1:
             dist.barrier(device_ids=[local])
 
+    # the LM head: split over the ranks by vocabulary rows (split.rs's optional N split, greedy token
+    # through cpq_tp_ar_argmax) when the fused all-reduce runs, else mirrored (split.rs's default)
+    import dataclasses
+    split_head = world > 1 and not args.nccl and not args.mirrored_head
+    hp = dataclasses.replace(tp.HP_BENCH_27B, split_output=True) if split_head else tp.HP_BENCH_27B
     parity = None
     if world > 1 and not args.no_parity:
-        parity = tp_parity(torch, st, tp, comm, exchange, rank, world)
+        parity = tp_parity(torch, st, tp, comm, exchange, rank, world, hp=hp)
         ok = [parity.get("ok", True) if rank == 0 else True]
         dist.broadcast_object_list(ok, src=0)
         if not ok[0]:
@@ -704,7 +714,7 @@ def main() -> int:
     # all-reduce waits dominate); one call per projection below, where it is the faster path
     use_trunk = args.m == 1 and not args.nccl and (args.trunk or (world >= 4 and not args.per_call))
     t_build = time.perf_counter()
-    stack = st.Stack(tp.HP_BENCH_27B, args.layers, rank, world, comm, m=args.m, seed=0,
+    stack = st.Stack(hp, args.layers, rank, world, comm, m=args.m, seed=0,
                      ar_exchange=exchange if (world > 1 and not args.nccl) else None, use_trunk=use_trunk)
     g = torch.Generator(device="cpu").manual_seed(1234)
     h0 = torch.randn(args.m, 5120, generator=g).cuda()
@@ -788,7 +798,7 @@ def main() -> int:
     torch.cuda.empty_cache()
     if not args.no_verify:
         vms = verify_step(torch, st, tp, args.layers, rank, world, comm, barrier,
-                          exchange=exchange if (world > 1 and not args.nccl) else None)
+                          exchange=exchange if (world > 1 and not args.nccl) else None, hp=hp)
         tv = torch.tensor([vms], dtype=torch.float64, device="cuda")
         if world > 1:
             dist.all_reduce(tv, op=dist.ReduceOp.MAX)
@@ -815,7 +825,9 @@ def main() -> int:
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8 dots (Q4_K/Q6_K x Q8_K), fp32 accumulate", "data": "synthetic",
         "config": {"workload": "27B-shaped stack decode (BASELINE config 5): 64 x Q4_K q/k/v/o/gate/up/down + "
-                               "mirrored Q6_K head [151936x5120], M=1, TP=N",
+                               "Q6_K head [151936x5120], M=1, TP=N",
+                   "head": ("split over the ranks by vocabulary rows, greedy token through cpq_tp_ar_argmax"
+                            if split_head else "mirrored" if world > 1 else "whole"),
                    "path": path,
                    "tp_allreduce": ar_mode,
                    "layers": args.layers, "m": args.m, "tp": world, "hidden": 5120, "ffn": 17408,

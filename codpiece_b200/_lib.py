@@ -33,7 +33,7 @@ EXPORTED = [
     "cpq_gguf_open", "cpq_gguf_close", "cpq_gguf_n_tensors", "cpq_gguf_find_tensor", "cpq_gguf_tensor_at",
     "cpq_gguf_get_u64", "cpq_gguf_get_str", "cpq_gguf_shard_shape", "cpq_gguf_read_shard", "cpq_gguf_load_shard",
     "cpq_tp_split_state", "cpq_tp_unique_id", "cpq_tp_comm_init", "cpq_tp_allreduce_f32", "cpq_tp_comm_check",
-    "cpq_tp_comm_destroy", "cpq_tp_ar_create", "cpq_tp_ar_connect", "cpq_tp_ar_destroy", "cpq_tp_ar_add", "cpq_tp_ar_zero", "cpq_mul_mat_fused_ar",
+    "cpq_tp_comm_destroy", "cpq_tp_ar_create", "cpq_tp_ar_connect", "cpq_tp_ar_destroy", "cpq_tp_ar_add", "cpq_tp_ar_zero", "cpq_tp_ar_argmax", "cpq_mul_mat_fused_ar",
     "cpq_synth_weights", "cpq_device_status", "cpq_set_wait_limit_ns", "cpq_last_error", "cpq_status_string",
     "cpq_abi_version",
 ]
@@ -138,6 +138,7 @@ def lib() -> C.CDLL:
         "cpq_tp_ar_destroy": (None, [vp]),
         "cpq_tp_ar_add": (st, [vp, vp, vp, i64, i64, vp]),
         "cpq_tp_ar_zero": (st, [vp, i64, i64, vp]),
+        "cpq_tp_ar_argmax": (st, [vp, vp, i64, i64, i64, i64, vp, vp]),
         "cpq_mul_mat_fused_ar": (st, [P(P(CpqTensor)), P(P(CpqTensor)), C.c_int, P(CpqTensor), P(CpqPrologue), vp, vp,
                                       vp]),
         "cpq_synth_weights": (st, [i32, vp, i64, i64, sz, C.c_uint64, i64, i64, vp]),

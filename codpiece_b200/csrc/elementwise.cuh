@@ -248,6 +248,57 @@ __global__ void __launch_bounds__(256, 1) ar_add_kernel(const ArIn ar, const flo
     if (threadIdx.x == 0) ar_consumer_end(ar, ticket, seq);  // thread 0's e0 is always < k
 }
 
+// Greedy token over a vocabulary split across ranks (the LM head's N split):
+// each CTA takes one token row, reduces this rank's logits [n] to (max, first
+// index), publishes it as two LL words (value bits, row0 + index) to every
+// rank's buffer (the producer side of the channel), then reads every rank's
+// pair and keeps the largest value, the lowest global index on ties (the
+// argmax of the unsplit row). grid m, 1024 threads.
+__global__ void __launch_bounds__(1024) ar_argmax_kernel(const ArIn in, const ArOut out, const float *__restrict__ x,
+                                                        int64_t n, int64_t ld, int64_t row0, int32_t *__restrict__ res) {
+    pdl_wait();
+    pdl_launch_dependents();
+    __shared__ unsigned seq;
+    __shared__ float sv[32];
+    __shared__ int32_t si[32];
+    unsigned ticket = 0;
+    if (threadIdx.x == 0) seq = ar_consumer_begin(in, ticket);  // = the producers' sequence number
+    const int t = blockIdx.x;
+    const float *xr = x + int64_t(t) * ld;
+    float best = -INFINITY;
+    int32_t bi = 0x7fffffff;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) argmax_merge(best, bi, xr[i], int32_t(i));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        argmax_merge(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
+    if ((threadIdx.x & 31) == 0) {
+        sv[threadIdx.x >> 5] = best;
+        si[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    for (int w = 1; w < int(blockDim.x >> 5); w++) argmax_merge(best, bi, sv[w], si[w]);
+    const unsigned e = seq;
+    const int64_t slot = int64_t(e % kArSlots) * out.world;
+    const uint64_t wv = (uint64_t(e) << 32) | __float_as_uint(best);
+    const uint64_t wi = (uint64_t(e) << 32) | uint32_t(int32_t(row0) + (bi == 0x7fffffff ? 0 : bi));
+    for (int d = 0; d < out.world; d++) {
+        uint64_t *dst = out.peer[d] + (slot + out.rank) * out.n_max + 2 * t;
+        st_relaxed_sys_u64(dst, wv);
+        st_relaxed_sys_u64(dst + 1, wi);
+    }
+    float gb = -INFINITY;
+    int32_t gi = 0x7fffffff;
+    for (int r = 0; r < in.world; r++) {
+        const uint64_t *src = in.base + (slot + r) * in.n_max + 2 * t;
+        const float v = ar_word(src, e);
+        const int32_t ix = int32_t(__float_as_uint(ar_word(src + 1, e)));
+        argmax_merge(gb, gi, v, ix);
+    }
+    res[t] = gi == 0x7fffffff ? 0 : gi;
+    ar_consumer_end(in, ticket, seq);
+}
+
 // A zero contribution to the next all-reduce (this rank's slot of every
 // rank's buffer): the producer side of row_block_out with all values 0.
 __global__ void __launch_bounds__(256) ar_zero_kernel(const ArOut ar, int64_t total) {

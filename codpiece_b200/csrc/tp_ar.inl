@@ -155,6 +155,23 @@ extern "C" cpq_status cpq_tp_ar_add(cpq_tp_ar *ar, const float *x, float *out, i
     return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "cpq_tp_ar_add: launch");
 }
 
+extern "C" cpq_status cpq_tp_ar_argmax(cpq_tp_ar *ar, const float *logits, int64_t n, int64_t m, int64_t ld,
+                                       int64_t row0, int32_t *out, void *stream) {
+    using namespace cpq;
+    if (!ar || !logits || !out) return fail(CPQ_ERR_INVALID_ARG, "cpq_tp_ar_argmax: null argument");
+    if (n <= 0 || m <= 0 || ld < n || row0 < 0 || row0 + n > 2147483647 || m > 65535)
+        return fail(CPQ_ERR_INVALID_ARG, "cpq_tp_ar_argmax: n=%lld m=%lld ld=%lld row0=%lld", (long long)n,
+                    (long long)m, (long long)ld, (long long)row0);
+    const char *why = "";
+    if (!ar_ready(ar, 2 * m, &why)) return fail(CPQ_ERR_INVALID_ARG, "cpq_tp_ar_argmax: %s", why);
+    ArIn in = ar_in_of(ar, 2);
+    in.n_ctas = unsigned(m);
+    const ArOut o = ar_out_of(ar, 2);
+    const cudaError_t e = launch(ar_argmax_kernel, dim3(unsigned(m)), dim3(1024), 0, static_cast<cudaStream_t>(stream),
+                                 in, o, logits, n, ld, row0, out);
+    return e == cudaSuccess ? CPQ_SUCCESS : cuda_fail(e, "cpq_tp_ar_argmax: launch");
+}
+
 extern "C" cpq_status cpq_tp_ar_zero(cpq_tp_ar *ar, int64_t n, int64_t m, void *stream) {
     using namespace cpq;
     if (!ar) return fail(CPQ_ERR_INVALID_ARG, "cpq_tp_ar_zero: null channel");

@@ -407,6 +407,14 @@ class ArChannel:
         """Contribute zeros (m tokens x n) to the next all-reduce (a rank without rows of it)."""
         check(lib().cpq_tp_ar_zero(self.handle, n, m, _stream(stream)), "cpq_tp_ar_zero")
 
+    def argmax(self, logits: torch.Tensor, row0: int, out: torch.Tensor, stream=None) -> torch.Tensor:
+        """Greedy tokens when the vocabulary is split across ranks: logits [m, n] are this rank's
+        rows row0 .. row0 + n - 1; out[m] (int32) = the global argmax (lowest index on ties)."""
+        m, n = logits.shape
+        check(lib().cpq_tp_ar_argmax(self.handle, C.c_void_p(logits.data_ptr()), n, m, logits.stride(0), int(row0),
+                                     C.c_void_p(out.data_ptr()), _stream(stream)), "cpq_tp_ar_argmax")
+        return out
+
     def close(self) -> None:
         if self.handle:
             lib().cpq_tp_ar_destroy(self.handle)

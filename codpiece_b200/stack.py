@@ -113,8 +113,15 @@ class Stack:
             self.layers.append(LayerWeights(
                 q=rows("q", q0, q1), k=rows("k", k0, k1), v=rows("v", v0, v1), o=kslice("o", e, o0, o1),
                 gate=rows("gate", f0, f1), up=rows("up", f0, f1), down=kslice("down", e, d0, d1)))
-        self.head = (mm.synth_weights(mm.TYPE_Q6_K, e, hp.n_vocab, tensor_seed(seed, 0, "head"), device=self.dev)
-                     if head else None)
+        # the head: mirrored (split.rs's default) or, with hp.split_output, this rank's rows of the
+        # vocabulary (split.rs's N split), the greedy token then found across ranks (cpq_tp_ar_argmax)
+        self.head_row0, n_head = 0, hp.n_vocab
+        if head and hp.split_output and world > 1:
+            ext = tp.split_state("output.weight", hp, hp.n_vocab, 256, world).ne[:world]
+            self.head_row0, n_head = int(sum(ext[:rank])), int(ext[rank])
+        self.head = (mm.synth_weights(mm.TYPE_Q6_K, e, n_head, tensor_seed(seed, 0, "head"), row0=self.head_row0,
+                                      device=self.dev) if head else None)
+        self.split_head = head and n_head != hp.n_vocab
         del nb_e
         f = lambda n: torch.zeros(m, n, dtype=torch.float32, device=self.dev)  # noqa: E731
         qmax = max((s.q[rank][1] - s.q[rank][0]) for s in self.shards) or 1
@@ -125,7 +132,7 @@ class Stack:
         self.qb, self.kb, self.vb = f(qmax), f(kmax), f(kmax)
         self.part = f(e)
         self.gb, self.ub, self.act = f(fmax), f(fmax), f(fmax)
-        self.logits = f(hp.n_vocab) if head else None
+        self.logits = f(n_head) if head else None
         self.tok = torch.zeros(m, dtype=torch.int32, device=self.dev)
         mm.init(self.dev.index, 64 << 20)
         self.graph: torch.cuda.CUDAGraph | None = None
@@ -137,6 +144,8 @@ class Stack:
         if ar_exchange is not None and world > 1 and m <= 16 and head:
             self.ar = mm.ArChannel(world, rank, m * e, self.dev.index)
             self.ar.connect(list(ar_exchange(self.ar.ipc_handle)))
+        if self.split_head and self.ar is None:
+            raise ValueError("a split LM head needs the fused all-reduce channel (ar_exchange) for its argmax")
         if use_plan:
             if world != 1 or m != 1:
                 raise ValueError("decode plans run the single-GPU M = 1 step")
@@ -243,7 +252,7 @@ class Stack:
             self.trunk.run(h, h_alt)
             if self.head is not None:
                 mm.mul_mat_fused([self.head], h_alt, [self.logits], mode=mm.PRO_RMS, eps=self.eps)
-                mm.argmax(self.logits, out=self.tok)
+                self._argmax()
             self.h_final = h_alt
             return
         if self.plan is not None:
@@ -310,7 +319,7 @@ class Stack:
                 mm.mul_mat_fused([self.head], h, [self.logits], mode=mm.PRO_RMS, r=self.part, h_out=h_alt,
                                  eps=self.eps)
             h, h_alt = h_alt, h
-            mm.argmax(self.logits, out=self.tok)
+            self._argmax()
         elif part_live:
             mm.add_(h, self.part)
         self.h_final = h
@@ -330,6 +339,13 @@ class Stack:
 
     def replay(self) -> None:
         self.graph.replay()
+
+    def _argmax(self) -> None:
+        """The greedy token: over this rank's logits, or across ranks when the head is split."""
+        if self.split_head:
+            self.ar.argmax(self.logits, self.head_row0, self.tok)
+        else:
+            mm.argmax(self.logits, out=self.tok)
 
     def _head_prologue_ar(self, h, h_out) -> None:
         """h_out = h + allreduce(part) for the Q6_K head (outside the Q4_K decode GEMV)."""

@@ -306,6 +306,14 @@ cpq_status cpq_tp_ar_add(cpq_tp_ar *ar, const float *x, float *out, int64_t k, i
  * (at TP8 the attention split leaves half of the ranks without attention
  * rows), so every rank still produces into every all-reduce. */
 cpq_status cpq_tp_ar_zero(cpq_tp_ar *ar, int64_t n, int64_t m, void *stream);
+/* The greedy token of each of m rows when the LM head's rows (the vocabulary)
+ * are split across the ranks (split.rs's optional N split of output.weight):
+ * every rank passes its logits [m][ld] (n of them per row, global indices
+ * row0 .. row0 + n - 1) and gets out[m] = the index of the largest logit of
+ * the whole row, the lowest index on ties: each rank's (max, index) pair
+ * crosses NVLink as LL words through the channel, one exchange, no NCCL. */
+cpq_status cpq_tp_ar_argmax(cpq_tp_ar *ar, const float *logits, int64_t n, int64_t m, int64_t ld, int64_t row0,
+                            int32_t *out, void *stream);
 
 /* cpq_mul_mat_fused with a channel at either end (either may be NULL):
  *  y_ar  Y_0 (n_w must be 1) is all-reduced through the channel instead of

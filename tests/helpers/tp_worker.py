@@ -1,7 +1,9 @@
 """One rank of the tensor-parallel stack check (launched by tests/test_gpu_tp.py
 through torch.distributed.run, one process per GPU). Modes: "nccl" (per-call
 projections, NCCL all-reduce), "ar" (per-call, fused NVLink all-reduce),
-"trunk" (the persistent trunk kernel, all-reduce inside it).
+"trunk" (the persistent trunk kernel, all-reduce inside it), "split" (as
+"ar", with the LM head's vocabulary split over the ranks and the greedy
+token found across them, cpq_tp_ar_argmax).
 
 Every rank builds its shard of a few-layer 27B-shaped stack (split.rs rules,
 NCCL allreduce through libcpq), runs one decode/verify step, and rank 0 also
@@ -28,7 +30,7 @@ def main() -> int:
     layers = int(sys.argv[2]) if len(sys.argv) > 2 else 2
     m = int(sys.argv[3]) if len(sys.argv) > 3 else 1
     mode = sys.argv[4] if len(sys.argv) > 4 else "nccl"
-    fused_ar = mode in ("ar", "trunk")
+    fused_ar = mode in ("ar", "trunk", "split")
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
@@ -44,8 +46,11 @@ def main() -> int:
         dist.all_gather_object(got, handle)
         return got
 
-    s = st.Stack(tp.HP_BENCH_27B, layers, rank, world, comm, m=m, seed=5, ar_exchange=exchange if fused_ar else None,
+    import dataclasses
+    hp = dataclasses.replace(tp.HP_BENCH_27B, split_output=True) if mode == "split" else tp.HP_BENCH_27B
+    s = st.Stack(hp, layers, rank, world, comm, m=m, seed=5, ar_exchange=exchange if fused_ar else None,
                  use_trunk=mode == "trunk")
+    assert s.split_head == (mode == "split")
     assert (s.trunk is not None) == (mode == "trunk")
     assert (s.ar is not None) == fused_ar
     s.h.copy_(h0)
@@ -66,7 +71,7 @@ def main() -> int:
     logits_tp = s.logits.cpu().numpy()
     h_tp = s.h_final.cpu().numpy()
     tok_tp = s.tok.cpu().numpy()
-    # every rank ends with the same mirrored head output
+    # every rank ends with the same greedy tokens
     gathered = [None] * world
     dist.all_gather_object(gathered, tok_tp.tolist())
     verdict = {}
@@ -75,7 +80,8 @@ def main() -> int:
         ref.h.copy_(h0)
         ref.step_body()
         torch.cuda.synchronize()
-        lr, hr = ref.logits.cpu().numpy(), ref.h_final.cpu().numpy()
+        hr = ref.h_final.cpu().numpy()
+        lr = ref.logits.cpu().numpy()[:, :logits_tp.shape[1]]  # rank 0's rows of a split head
         verdict = {
             "world": world, "layers": layers, "m": m, "fused_ar": fused_ar, "mode": mode,
             "logits_rel": float(np.abs(logits_tp - lr).max() / np.abs(lr).max()),

@@ -36,7 +36,8 @@ def _ngpus():
                                                  (2, 3, 8, "ar"), (2, 2, 13, "ar"),
                                                  (2, 3, 1, "trunk"), (4, 2, 1, "ar"), (4, 3, 1, "trunk"),
                                                  (4, 2, 8, "ar"), (8, 2, 1, "ar"), (8, 3, 1, "trunk"),
-                                                 (8, 2, 8, "nccl"), (8, 3, 8, "ar")])
+                                                 (8, 2, 8, "nccl"), (8, 3, 8, "ar"),
+                                                 (2, 2, 1, "split"), (2, 2, 8, "split"), (8, 2, 1, "split")])
 def test_tensor_parallel_stack_matches_tp1(cuda, tmp_path, world, layers, m, mode):
     """mode "ar": the row-parallel partial sums go through the fused NVLink allreduce
     (cpq_mul_mat_fused_ar); "nccl": through cpq_tp_allreduce_f32; "trunk": the
@@ -51,7 +52,7 @@ def test_tensor_parallel_stack_matches_tp1(cuda, tmp_path, world, layers, m, mod
     res = subprocess.run(cmd, cwd=str(ROOT), env=env, capture_output=True, text=True)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     v = json.loads(out.read_text())
-    assert v["fused_ar"] == (mode in ("ar", "trunk")) and v["mode"] == mode
+    assert v["fused_ar"] == (mode in ("ar", "trunk", "split")) and v["mode"] == mode
     assert v["ranks_agree"]
     assert v["logits_rel"] <= TOL and v["h_rel"] <= TOL, v
     assert v["tok_tp"] == v["tok_ref"], v
