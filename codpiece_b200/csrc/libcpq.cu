@@ -10,7 +10,7 @@
 //   gemv_mma.cuh     Q4_K verify GEMM (M 4..16) on int8 mma tiles, stream-K
 //   act_prep.cuh     decode activation image: fused rms/swiglu prologue + Q8_K
 //   gemv_row.cuh     Q4_K decode GEMV (M 1..3), lane per row
-//   gemm_tc.cuh      Q4_K chunked-prefill GEMM (M > 16) on tcgen05 tensor cores
+//   gemm_tc.cuh      chunked-prefill GEMM (M > 16) on tcgen05 tensor cores: Q4_K, Q8_0, Q6_K
 //   decode.cuh       persistent decode step: a chain of Q4_K GEMV phases in one launch
 //   trunk.cuh        persistent decode trunk: every layer of a rank's step in one launch
 //   gdn.cuh          gated delta-net recurrence (the GDN layers' per-token state update)
