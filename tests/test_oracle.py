@@ -159,3 +159,32 @@ def test_empty_and_minimal_shapes(oracle):
     x = synth.activations(1, 256, seed=2)
     y = oracle.mul_mat(synth.Q4_K, w, 256, 3, x)
     assert y.shape == (1, 3) and np.isfinite(y).all()
+
+
+@pytest.mark.parametrize("qt", [synth.Q4_K, synth.Q6_K, synth.Q8_0])
+def test_block_dots_match_gguf_py_dequantization(oracle, qt):
+    """The integer block dots (scales, mins, the Q6_K -32 offset, bsums) against the
+    definition they implement: gguf-py's dequantized weights (llama.cpp's own Python
+    decoding of the formats) times the dequantized activation blocks d * q, summed in
+    float64. Only fp32 rounding separates the two."""
+    gg = pytest.importorskip("gguf")
+    from gguf import GGMLQuantizationType as T
+
+    gt = {synth.Q4_K: T.Q4_K, synth.Q6_K: T.Q6_K, synth.Q8_0: T.Q8_0}[qt]
+    n, k, m = 16, 2048, 3
+    w, x = synth.config_inputs(qt, n, k, m, seed=21)
+    wd = gg.quants.dequantize(w, gt).reshape(n, k).astype(np.float64)
+    xq = oracle.quantize_act(qt, x)                          # [m, row bytes] of Q8_K / Q8_0 blocks
+    if qt == synth.Q8_0:
+        blk = xq.reshape(m, k // 32, 34)
+        d = blk[:, :, :2].copy().view(np.float16).astype(np.float64)[..., 0]
+        q = blk[:, :, 2:].view(np.int8).astype(np.float64)
+        xd = (q * d[..., None]).reshape(m, k)
+    else:
+        blk = xq.reshape(m, k // 256, 292)
+        d = blk[:, :, :4].copy().view(np.float32).astype(np.float64)[..., 0]
+        q = blk[:, :, 4:260].view(np.int8).astype(np.float64)
+        xd = (q * d[..., None]).reshape(m, k)
+    ref = xd @ wd.T
+    y = oracle.mul_mat(qt, w, k, n, x).astype(np.float64)
+    assert np.abs(y - ref).max() <= 1e-5 * np.abs(ref).max()
