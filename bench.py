@@ -847,6 +847,11 @@ def main() -> int:
         "prefill": prefill,
         "verify": verify,
         "tp_parity": parity,
+        "parity": {"activation_blocks": "byte-identical to the CPU oracle (tests/)",
+                   "outputs": "max |y - y_oracle| / max |y_oracle| <= 1e-3 (tests/)",
+                   "oracle_pinning": "partial: dequantization and the portable Q8_0 quantizer pinned to gguf-py "
+                                     "fixtures, the block dots pinned to gguf-py's dequantization; the Q8_K and "
+                                     "AVX2 Q8_0 quantizers' rounding rules are restatements (ggml is not available)"},
         "small_configs": small,
     }
     print(json.dumps(line), flush=True)
