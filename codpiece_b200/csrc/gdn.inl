@@ -25,7 +25,7 @@ static int64_t nelem(const cpq_tensor *t) { return t->ne[0] * t->ne[1] * t->ne[2
 
 template <int SV, bool KDA>
 static cudaError_t launch_gdn_t(const GdnArgs &a, int64_t n_seqs, cudaStream_t st) {
-    constexpr int cols = SV < 32 ? SV : 32;
+    constexpr int cols = SV < kGdnCols ? SV : kGdnCols;
     return launch(gdn_kernel<SV, KDA>, dim3(unsigned(a.H), unsigned(n_seqs), unsigned(SV / cols)), dim3(cols * 4), 0, st,
                   a);
 }
