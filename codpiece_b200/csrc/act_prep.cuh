@@ -45,6 +45,12 @@ struct ActPrepArgs {
     float eps;
     uint8_t *out;      // the image (row_act_bytes(k, m) bytes)
     ArIn ar;           // RMS: r = the all-reduced residual of this channel (r must be null)
+    // the fragment-order image of the int8-MMA GEMV instead (act_prep_kernel<false, true>):
+    // quants [nbk][mp][4][8][8], split 32-sums [nbk][mp][16], scales [nbk][mp]; tokens m..mp-1 zero
+    int8_t *fq;
+    uint8_t *fb;
+    float *fd;
+    int mp;
 };
 
 template <bool L2>
@@ -90,19 +96,23 @@ __device__ __forceinline__ void act_load_v(int mode, const float *xr, const floa
 // Block b of token row t from its loaded values v: RMS scaling (and weight
 // g), the Q8_K quantizer, and the three parts of the activation image of m
 // rows (layout above). One warp.
+__device__ __forceinline__ void act_scale(int mode, float (&v)[8], float scale, const float *g, int b) {
+    if (mode != kActRms) return;
+    const int64_t e0 = int64_t(b) * kQK_K + (threadIdx.x & 31) * 8;
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = __fmul_rn(v[e], scale);
+    if (g) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = __fmul_rn(v[e], g[e0 + e]);
+    }
+}
+
 __device__ __forceinline__ void act_quantize_store(int mode, float (&v)[8], float scale, const float *g, int b, int t,
                                                    int64_t k, int m, uint8_t *img) {
     const int lane = threadIdx.x & 31;
     const int nbk = int(k / kQK_K);
     const int64_t e0 = int64_t(b) * kQK_K + lane * 8;
-    if (mode == kActRms) {
-#pragma unroll
-        for (int e = 0; e < 8; e++) v[e] = __fmul_rn(v[e], scale);
-        if (g) {
-#pragma unroll
-            for (int e = 0; e < 8; e++) v[e] = __fmul_rn(v[e], g[e0 + e]);
-        }
-    }
+    act_scale(mode, v, scale, g, b);
     int q[8];
     const float d = q8k_quantize_block(v, lane, q);
     uint32_t lo, hi;
@@ -122,6 +132,32 @@ __device__ __forceinline__ void act_quantize_store(int mode, float (&v)[8], floa
         bb[8 + (lane >> 2)] = uint8_t(int8_t(s32 >> 8));
     }
     if (lane == 0) dd[t * nbk + b] = d;
+}
+
+// The same for the fragment-order image (ActPrepArgs::fq/fb/fd): lane l's
+// elements 8l..8l+7 are sub-block l/4 at position 8(l%4), stored at
+// [b][t][l%4][l/4][8]; the 32-sum of sub-block s as its low byte at 16bt + s
+// and its high byte at 16bt + 8 + s; d at bt (bt = b * mp + t).
+__device__ __forceinline__ void act_quantize_store_frag(int mode, float (&v)[8], float scale, const float *g, int b,
+                                                        int t, const ActPrepArgs &a) {
+    const int lane = threadIdx.x & 31;
+    act_scale(mode, v, scale, g, b);
+    int q[8];
+    const float d = q8k_quantize_block(v, lane, q);
+    uint32_t lo, hi;
+    pack8(q, lo, hi);
+    const size_t bt = size_t(b) * a.mp + t;
+    *reinterpret_cast<uint2 *>(a.fq + bt * kQK_K + (lane & 3) * 64 + (lane >> 2) * 8) = make_uint2(lo, hi);
+    int s8 = 0;
+#pragma unroll
+    for (int e = 0; e < 8; e++) s8 += q[e];
+    int s32 = s8 + __shfl_xor_sync(0xffffffffu, s8, 1);
+    s32 += __shfl_xor_sync(0xffffffffu, s32, 2);
+    if ((lane & 3) == 0) {
+        a.fb[bt * 16 + (lane >> 2)] = uint8_t(s32 & 0xff);
+        a.fb[bt * 16 + 8 + (lane >> 2)] = uint8_t(int8_t(s32 >> 8));
+    }
+    if (lane == 0) a.fd[bt] = d;
 }
 
 __device__ __forceinline__ void store8(float *p, const float (&v)[8]) {
@@ -176,11 +212,14 @@ __device__ __forceinline__ bool act_rms_row(const float *xr, const float *rr, in
 // instance without it carries none of that code. Both stay small enough
 // (256 threads x at most 104 registers) to share an SM with a row-GEMV CTA
 // while they wait under programmatic dependent launch.
+// FRAG: the fragment-order image of the int8-MMA GEMV (verify, M = 4..16);
+// grid (ceil(nbk / 8), mp), the CTAs of tokens m..mp-1 store zero blocks.
 #ifndef CPQ_ACT_AR_MAXNREG
 #define CPQ_ACT_AR_MAXNREG 104
 #endif
-template <bool AR>
+template <bool AR, bool FRAG = false>
 __global__ void __launch_bounds__(256, 1) __maxnreg__(AR ? CPQ_ACT_AR_MAXNREG : 104) act_prep_kernel(const ActPrepArgs a) {
+    static_assert(!(AR && FRAG), "the fragment image is built without the all-reduce input");
     // Dependents (the row GEMV) may launch before this kernel even starts
     // waiting: they only prefetch weights until their own griddepcontrol.wait,
     // which still orders them after this kernel, and so they take each SM as
@@ -192,6 +231,14 @@ __global__ void __launch_bounds__(256, 1) __maxnreg__(AR ? CPQ_ACT_AR_MAXNREG : 
     const int warp = threadIdx.x >> 5;
     const int t = blockIdx.y;
     const int nbk = int(a.k / kQK_K);
+    if (FRAG && t >= a.m) {  // padding token (uniform over the CTA: no barrier is skipped by part of it)
+        const int bz = blockIdx.x * 8 + warp;
+        if (bz < nbk) {
+            float z[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+            act_quantize_store_frag(kActPlain, z, 1.0f, nullptr, bz, t, a);
+        }
+        return;
+    }
     const float *xr = a.x + t * a.x_stride;
     const float *rr = a.r ? a.r + t * a.x_stride : nullptr;
     ArRows rows;
@@ -227,7 +274,8 @@ __global__ void __launch_bounds__(256, 1) __maxnreg__(AR ? CPQ_ACT_AR_MAXNREG : 
     }
     if (a.mode == kActRms && (rr || arp) && a.h_out)
         store8(a.h_out + t * a.x_stride + int64_t(b) * kQK_K + (threadIdx.x & 31) * 8, v);
-    act_quantize_store(a.mode, v, scale, a.g, b, t, a.k, a.m, a.out);
+    if (FRAG) act_quantize_store_frag(a.mode, v, scale, a.g, b, t, a);
+    else act_quantize_store(a.mode, v, scale, a.g, b, t, a.k, a.m, a.out);
     if (AR && threadIdx.x == 0) ar_consumer_end(a.ar, ticket, ar_seq);  // thread 0's block is always < nbk
 }
 

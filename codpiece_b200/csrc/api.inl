@@ -676,8 +676,12 @@ static size_t act_region_bytes(int32_t vt, int64_t k, int64_t m) {
 
 // up != NULL: the input is silu(x) * up, formed inside the quantizer (x = gate rows).
 // ar_out: weight 0's outputs go to every rank through the fused all-reduce channel.
+// up: the SwiGLU prologue (silu(x) * up) inside the fragment quantizer; rms: the
+// RMS prologue, by act_prep_kernel<false, true> (the row's RMS, then the
+// fragment image, one launch; x, rms->r and rms->h_out 16-byte aligned rows).
 static cpq_status run_q4k_mma(const GemvArgs &g, const float *x, int64_t x_stride, int64_t m, uint8_t *ws,
-                              cudaStream_t st, const float *up = nullptr, const ArOut *ar_out = nullptr) {
+                              cudaStream_t st, const float *up = nullptr, const ArOut *ar_out = nullptr,
+                              const cpq_prologue *rms = nullptr) {
     const int64_t k = g.k, nbk = k / kQK_K;
     static thread_local MmaArgs a;  // large (tensor maps); filled per call
     std::memset(&a, 0, sizeof a);
@@ -709,11 +713,30 @@ static cpq_status run_q4k_mma(const GemvArgs &g, const float *x, int64_t x_strid
         int8_t *qs = reinterpret_cast<int8_t *>(act);
         uint8_t *bs = act + align_up(size_t(nbk) * mp * 256, 256);
         float *d = reinterpret_cast<float *>(bs + align_up(size_t(nbk) * mp * 16, 256));
-        const int64_t qwarps = nbk * mp;
-        cudaError_t e = launch(quantize_q8K_frag_kernel, dim3(unsigned(std::min<int64_t>((qwarps + 7) / 8, 65535))),
-                               dim3(256), 0, st, x + t0 * x_stride, k, mt, mp, x_stride, qs, bs, d,
-                               up ? up + t0 * x_stride : nullptr);
-        if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+        cudaError_t e;
+        if (rms) {
+            ActPrepArgs pa = {};
+            pa.mode = kActRms;
+            pa.x = x + t0 * x_stride;
+            pa.r = rms->r ? rms->r + t0 * x_stride : nullptr;
+            pa.g = rms->g;
+            pa.h_out = rms->h_out ? rms->h_out + t0 * x_stride : nullptr;
+            pa.x_stride = x_stride;
+            pa.k = k;
+            pa.m = mt;
+            pa.eps = rms->eps;
+            pa.fq = qs;
+            pa.fb = bs;
+            pa.fd = d;
+            pa.mp = mp;
+            e = launch(act_prep_kernel<false, true>, dim3(unsigned((nbk + 7) / 8), unsigned(mp)), dim3(256), 0, st, pa);
+            if (e != cudaSuccess) return cuda_fail(e, "act_prep launch");
+        } else {
+            const int64_t qwarps = nbk * mp;
+            e = launch(quantize_q8K_frag_kernel, dim3(unsigned(std::min<int64_t>((qwarps + 7) / 8, 65535))), dim3(256),
+                       0, st, x + t0 * x_stride, k, mt, mp, x_stride, qs, bs, d, up ? up + t0 * x_stride : nullptr);
+            if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+        }
         a.m = mt;
         a.act.qs = qs;
         a.act.bs = bs;
@@ -1058,6 +1081,9 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
     if (pro.mode == CPQ_PRO_SWIGLU && s0.wtype == CPQ_TYPE_Q4_K && m <= kMmaMaxTokens && aligned(xp, 16) &&
         x_stride % 4 == 0)
         return run_q4k_mma(a, xp, x_stride, m, wsb, st, pro.r, mma_ar_p);  // SwiGLU inside the quantizer
+    if (pro.mode == CPQ_PRO_RMS && s0.wtype == CPQ_TYPE_Q4_K && m <= kMmaMaxTokens && aligned(xp, 16) &&
+        x_stride % 4 == 0)
+        return run_q4k_mma(a, xp, x_stride, m, wsb, st, nullptr, mma_ar_p, &pro);  // RMS + image in one launch
     if (pro.mode != CPQ_PRO_NONE) {
         // the other paths quantize an fp32 input: apply the prologue into the workspace first
         float *tmp = reinterpret_cast<float *>(wsb + kWsActOffset + act_region_bytes(vt, s0.k, m));
