@@ -329,12 +329,12 @@ static bool q8_rows_ok(const GemvArgs &g, int mt) {
     const int mr = mt <= 2 ? mt : mt <= 4 ? 4 : 8;
     return g.n_w == 1 && g.k % 256 == 0 && n % 2 == 0 && n > 0 && g.rs == size_t(nb) * kQ8_0_Bytes &&
            aligned(g.w[0], 16) && aligned(g.act.qs, 16) && aligned(g.act.d, 16) && mt <= 8 &&
-           q8r_smem_bytes(int(nb), mr) <= kSmemMax;
+           q8r_smem_bytes(int(nb), mr, 4, 2) <= kSmemMax;  // the narrowest instance of launch_q8_rows_t
 }
 
-template <int MT, bool QX = false>
-static cudaError_t launch_q8_rows_t(const Q8RowArgs &a, cudaStream_t st) {
-    auto kern = gemv_q8_0_rows_kernel<MT, QX>;
+template <int MT, bool QX, int W, int S>
+static cudaError_t launch_q8_rows_ws(const Q8RowArgs &a, cudaStream_t st) {
+    auto kern = gemv_q8_0_rows_kernel<MT, QX, W, S>;
     const int dev = current_device();
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     static std::atomic<int> set[kMaxDevices];
@@ -344,8 +344,20 @@ static cudaError_t launch_q8_rows_t(const Q8RowArgs &a, cudaStream_t st) {
         set[dev].store(1, std::memory_order_relaxed);
     }
     const int64_t pairs = a.n / 2;
-    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), (pairs + kQ8rWarps - 1) / kQ8rWarps));
-    return launch(kern, dim3(unsigned(grid)), dim3(kQ8rWarps * 32), size_t(q8r_smem_bytes(a.nb, MT)), st, a);
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), (pairs + W - 1) / W));
+    return launch(kern, dim3(unsigned(grid)), dim3(W * 32), size_t(q8r_smem_bytes(a.nb, MT, W, S)), st, a);
+}
+
+// The widest ring that fits in shared memory: 8 warps x 2 stages, else 6 or
+// 4 warps (K = 6144 at M = 3..8 needs 6: [6144 x 6144] at M = 4 42.6 -> 22.8 us
+// against the generic kernel it fell back to). A deeper 6 x 3 ring for one
+// token (every pair of [5120 x 5120] in flight at once) measured slower:
+// 10.7 vs 10.0 us.
+template <int MT, bool QX = false>
+static cudaError_t launch_q8_rows_t(const Q8RowArgs &a, cudaStream_t st) {
+    if (q8r_smem_bytes(a.nb, MT, kQ8rWarps, 2) <= kSmemMax) return launch_q8_rows_ws<MT, QX, kQ8rWarps, 2>(a, st);
+    if (q8r_smem_bytes(a.nb, MT, 6, 2) <= kSmemMax) return launch_q8_rows_ws<MT, QX, 6, 2>(a, st);
+    return launch_q8_rows_ws<MT, QX, 4, 2>(a, st);
 }
 
 // x != NULL: the kernel quantizes the fp32 activations itself (no quantizer launch).

@@ -255,10 +255,10 @@ __host__ __device__ constexpr int q8r_bar_bytes() { return 128 * ((kQ8rWarps * 3
 __host__ __device__ constexpr int q8r_act_bytes(int nb, int m) {
     return int(align_up(size_t(m) * nb * kQK8_0, 16) + align_up(size_t(m) * nb * 4, 16));
 }
-__host__ __device__ constexpr int q8r_stages(int) { return 2; }  // two 10.9 KB stages per warp at K = 5120
 // + 16 bytes: the last block's quants are read with aligned 4-byte loads that reach 2 bytes past it
-__host__ __device__ constexpr int q8r_smem_bytes(int nb, int m) {
-    return q8r_bar_bytes() + q8r_act_bytes(nb, m) + kQ8rWarps * q8r_stages(m) * q8r_stage_bytes(nb) + 16;
+// (w warps of s stages; the barrier area holds up to kQ8rWarps * 3 stage barriers)
+__host__ __device__ constexpr int q8r_smem_bytes(int nb, int m, int w = kQ8rWarps, int s = 2) {
+    return q8r_bar_bytes() + q8r_act_bytes(nb, m) + w * s * q8r_stage_bytes(nb) + 16;
 }
 __device__ __forceinline__ int q8r_swz(int s) { return s ^ ((s >> 3) & 1); }
 
@@ -310,10 +310,10 @@ __device__ __forceinline__ void q8r_quantize_into(const Q8RowArgs &a, int8_t *xq
 }
 
 // QX: the activations arrive as fp32 and are quantized here (a.x) instead of
-// by a separate quantizer launch (a.qs, a.d).
-template <int MT, bool QX = false>
-__global__ void __launch_bounds__(kQ8rWarps * 32, 1) gemv_q8_0_rows_kernel(const __grid_constant__ Q8RowArgs a) {
-    constexpr int S = q8r_stages(MT);
+// by a separate quantizer launch (a.qs, a.d). W warps of S ring stages.
+template <int MT, bool QX = false, int W = kQ8rWarps, int S = 2>
+__global__ void __launch_bounds__(W * 32, 1) gemv_q8_0_rows_kernel(const __grid_constant__ Q8RowArgs a) {
+    static_assert(W * S <= kQ8rWarps * 3, "stage barriers");
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nb = a.nb;
@@ -335,8 +335,8 @@ __global__ void __launch_bounds__(kQ8rWarps * 32, 1) gemv_q8_0_rows_kernel(const
     __syncthreads();
 
     const int64_t npairs = a.n / 2;
-    const int64_t G = int64_t(gridDim.x) * kQ8rWarps;
-    const int64_t g = int64_t(blockIdx.x) * kQ8rWarps + warp;
+    const int64_t G = int64_t(gridDim.x) * W;
+    const int64_t g = int64_t(blockIdx.x) * W + warp;
     const int64_t p_begin = g * npairs / G, p_end = (g + 1) * npairs / G;
     const uint64_t policy = l2_policy_evict_first();
     int64_t p_issue = p_begin;

@@ -83,6 +83,12 @@ CASES = [
     (synth.Q8_0, 1002, 2048, 3),
     (synth.Q8_0, 64, 256, 8),
     (synth.Q8_0, 1000, 5120, 12),
+    # narrower rings when 8 warps x 2 stages do not fit: 6 x 2 (K = 6144 at M = 4 and 8, K = 8192
+    # at M = 2) and 4 x 2 (K = 10240, the token quantized in-kernel)
+    (synth.Q8_0, 6144, 6144, 4),
+    (synth.Q8_0, 2000, 6144, 8),
+    (synth.Q8_0, 1002, 8192, 2),
+    (synth.Q8_0, 500, 10240, 1),
     (synth.Q4_K, 300, 2048, 40),
 ]
 
