@@ -40,17 +40,21 @@
 //               loads complete on rank 0's "fullB"
 //   warp 2      one lane TMA-loads this CTA's raw Q4_K superblocks (box 128
 //               rows x 144 bytes) into its raw ring ("rawFull"/"rawEmpty")
-//   warps 4-11  dequantize: warp w owns TMEM lanes (rows) 32*(w%4)..+31, warps
-//               4-7 the first half of every superblock (even stages), 8-11
-//               the second half (odd stages); a thread turns its row's 64
-//               bytes of nibbles into 128 fp16 and stores them as 64 columns
-//               with tcgen05.st; each warp arrives on rank 0's
-//               "fullA" (8 arrivals per stage, 4 per CTA; a plain remote
-//               arrive: the operand lives in tensor memory, ordered by the
-//               tcgen05 fences, so no cluster-scope memory fence is needed).
-//               After the K loop they read
-//               the CTA's accumulator (tcgen05.ld 32x32b), warps 4-7 the first
-//               half of the token columns, 8-11 the second, and store Y.
+//   warps 4-15  dequantize, in kTcDqGroups = 3 groups of 4: warp w owns TMEM
+//               lanes (rows) 32*(w%4)..+31, group g = (w-4)/4 the stages s
+//               with s % 3 == g (a stage is half a superblock, s % 2 says
+//               which); a thread turns its row's 64 bytes of nibbles into
+//               128 fp16 and stores them as 64 columns with tcgen05.st; each
+//               warp arrives on rank 0's "fullA" (8 arrivals per stage, 4
+//               per CTA; a plain remote arrive: the operand lives in tensor
+//               memory, ordered by the tcgen05 fences, so no cluster-scope
+//               memory fence is needed). Three groups instead of two: the
+//               Q4_K FFN shapes at M = 512 and 2048, FLOP-weighted, 0.571
+//               -> 0.587 of the bf16 peak, Q6_K at M = 512 +9-10 % (the
+//               dequantization is latency-bound per warp).
+//               After the K loop they read the CTA's accumulator
+//               (tcgen05.ld 32x32b), group g a third of the token columns,
+//               and store Y.
 // Waits are bounded (wait_limit_ns()); a timeout sets g_dev_error and a CTA-wide
 // abort flag, every role skips to the end, the TMA lanes wait (bounded) for
 // their copies in flight, the MMA lane for its last commit, and the TMEM is
@@ -87,8 +91,15 @@ constexpr uint32_t kTcAccCols = 256;           // accumulator columns (tile_n <=
 constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcAStageCols = kTcK / 2;  // two fp16 per 32-bit column
 static_assert(kTcAccCols + kTcAStageCols * kTcAStages <= kTcTmemCols, "TMEM columns");
-constexpr int kTcThreads = 384;  // 4 role warps + 8 dequantizing warps
-constexpr int kTcDqWarps = 8;
+// Dequantizing warps come in groups of 4 (one per TMEM lane quarter); group g
+// takes the stages s with s % kTcDqGroups == g.
+#ifndef CPQ_TC_DQ_GROUPS
+#define CPQ_TC_DQ_GROUPS 3
+#endif
+constexpr int kTcDqGroups = CPQ_TC_DQ_GROUPS;
+static_assert(kTcDqGroups >= 2 && kTcDqGroups <= 3, "dequant groups (512 threads at most: 128 registers)");
+constexpr int kTcThreads = 128 + 128 * kTcDqGroups;  // 4 role warps + the dequantizing warps
+constexpr int kTcDqWarps = 8;                        // arrivals per A stage: one group of 4 warps in each CTA
 constexpr int kTcBAtomBytes = kTcMaxTok / 2 * 128;  // one swizzle atom column of the CTA's half
 constexpr int kTcBBytes = kTcBAtomBytes * (kTcK / kTcAtomK);
 
@@ -403,8 +414,8 @@ __device__ __forceinline__ void dq_q6_k_stage(const uint8_t *win, int sh, int gr
 // its raw bytes come from HBM about once. Stage, slot and parity counters run
 // across tiles, so the producers stream straight into the next tile; the
 // accumulator is handed between the MMA issuer and the epilogue with
-// acc_full (multicast commit) and acc_empty (8 epilogue warps of each CTA
-// arrive on rank 0).
+// acc_full (multicast commit) and acc_empty (the 12 epilogue warps of each
+// CTA arrive on rank 0).
 template <int WT>
 __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
     constexpr int kSlots = TcW<WT>::kSlots, kRaw = tc_raw_bytes<WT>();
@@ -450,7 +461,7 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
             mbar_init(&rawEmpty[s], kTcDqWarps);
         }
         mbar_init(acc_full, 1);
-        mbar_init(acc_empty, 2 * kTcDqWarps);  // rank 0: every epilogue warp of both CTAs
+        mbar_init(acc_empty, 2 * 4 * kTcDqGroups);  // rank 0: every epilogue warp of both CTAs
         // a wait on this device has already timed out: do no work (the error stays reported)
         *abort_flag = (*reinterpret_cast<volatile uint32_t *>(&g_dev_error) & kDevErrWaitTimeout) ? 1 : 0;
         fence_mbar_init();
@@ -580,20 +591,21 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
     } else if (warp >= 4) {
         // ---- dequantization + epilogue (rows past n arrive zero-filled, so they dequantize to 0) ----
         const int dq = warp - 4;
-        const int grp = dq >> 2;                      // superblock half (= stage parity) of this warp
+        const int grp = dq >> 2;                      // this warp's group: stages s % kTcDqGroups == grp
         const int quarter = warp & 3;                 // TMEM lane quarter this warp may access
         const int r = 32 * quarter + lane;            // slot row = TMEM lane
         // the tile row it holds (Q6_K slots hold the rows grouped by box)
         const int row_of_lane = WT == CPQ_TYPE_Q6_K ? a.q6_l * (r % (kTcRows / a.q6_l)) + r / (kTcRows / a.q6_l) : r;
         const uint32_t lane_base = uint32_t(32 * quarter) << 16;
         const uint32_t acc_empty0 = cluster_addr(acc_empty, 0);
-        int64_t gs = 0;   // stages of all tiles so far (this warp handles those with gs % 2 == grp)
+        int64_t gs = 0;   // stages of all tiles so far (an even count: two per superblock)
         int64_t gr = 0;   // superblocks of all tiles so far
         bool ok = true;
 
-        // One stage: dequantize superblock half grp of stage t into A slot gs % kTcAStages.
+        // One stage: dequantize superblock half g_stage % 2 of the stage into A slot g_stage % kTcAStages.
         // kb: the superblock's index in the row; row0: the tile's first row of this CTA.
         auto dequant_stage = [&](int64_t g_stage, int64_t g_sb, int kb, int64_t row0) -> bool {
+            const int hf = int(g_stage & 1);  // superblock half
             const int sa = int(g_stage % kTcAStages);
             const uint32_t pa = uint32_t(g_stage / kTcAStages) & 1u;
             const int rs = int(g_sb % kSlots);
@@ -603,13 +615,13 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
                 uint32_t v[2][32];
                 const uint8_t *raw = sRaw + rs * kRaw + r * TcW<WT>::kRowBytes;
                 if constexpr (WT == CPQ_TYPE_Q8_0) {
-                    if (grp) dq_q8_0_stage<1>(raw, v);
+                    if (hf) dq_q8_0_stage<1>(raw, v);
                     else dq_q8_0_stage<0>(raw, v);
                 } else {
                     // where the superblock starts inside this row's window (the copy began 16-aligned)
                     const int j = r / (kTcRows / a.q6_l);  // the box (member of the row group)
                     const int sh = int((uint64_t(j) * uint64_t(a.w_rs) + uint64_t(kb) * kQ6K_Bytes) & 15u);
-                    dq_q6_k_stage(raw, sh, grp, v);
+                    dq_q6_k_stage(raw, sh, hf, v);
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&rawEmpty[rs]);  // this warp is done with the slot
@@ -629,13 +641,13 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
             const uint4 hd = *reinterpret_cast<const uint4 *>(raw);
             uint4 qv[4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) qv[i] = *reinterpret_cast<const uint4 *>(raw + 16 + 64 * grp + 16 * i);
+            for (int i = 0; i < 4; i++) qv[i] = *reinterpret_cast<const uint4 *>(raw + 16 + 64 * hf + 16 * i);
             __syncwarp();
             if (lane == 0) mbar_arrive(&rawEmpty[rs]);  // this warp is done with the superblock
-            // scales/mins of sub-blocks 4*grp .. 4*grp+3 (get_scale_min_k4): bytes of these words
-            const uint32_t scw = grp == 0 ? (hd.y & 0x3f3f3f3fu) : ((hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u));
+            // scales/mins of sub-blocks 4*hf .. 4*hf+3 (get_scale_min_k4): bytes of these words
+            const uint32_t scw = hf == 0 ? (hd.y & 0x3f3f3f3fu) : ((hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u));
             const uint32_t mnw =
-                grp == 0 ? (hd.z & 0x3f3f3f3fu) : (((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u));
+                hf == 0 ? (hd.z & 0x3f3f3f3fu) : (((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u));
             const float d = half_bits_to_float(hd.x), dmin = half_bits_to_float(hd.x >> 16);
             if (!__all_sync(0xffffffffu, tc_wait(&emptyA[sa], pa ^ 1u, abort_flag))) return false;
             tc_fence_after();  // the MMAs that read this A stage have completed
@@ -643,7 +655,7 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
             uint32_t v[2][32];
 #pragma unroll
             for (int p = 0; p < 2; p++) {
-                // 32 bytes of nibbles: low nibbles = sub-block 4*grp+2p, high = 4*grp+2p+1
+                // 32 bytes of nibbles: low nibbles = sub-block 4*hf+2p, high = 4*hf+2p+1
                 const int sh = 16 * p;
                 const __half2 slo = __float2half2_rn(d * float((scw >> sh) & 0xffu));
                 const __half2 shi = __float2half2_rn(d * float((scw >> (sh + 8)) & 0xffu));
@@ -684,8 +696,9 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
             // a K range's partial products go to its own plane of part; a whole K to Y
             float *yb = ks_n > 1 ? a.part + (tile % ks_n) * a.m * a.n : a.y;
             const int64_t ys = ks_n > 1 ? a.n : a.y_stride;
-            const int half = (((tile_n + 1) / 2) + 31) & ~31;
-            const int cbeg = grp * half, cend = grp ? tile_n : (half < tile_n ? half : tile_n);
+            // group grp drains columns [grp * part, (grp + 1) * part) (part a multiple of 32)
+            const int part = (((tile_n + kTcDqGroups - 1) / kTcDqGroups) + 31) & ~31;
+            const int cbeg = grp * part, cend = (grp + 1) * part < tile_n ? (grp + 1) * part : tile_n;
             for (int c0 = cbeg; c0 < cend && tok0 + c0 < tend; c0 += 32) {
                 float v[32];
                 tmem_ld32(tmem + lane_base + uint32_t(c0), v);
@@ -709,13 +722,13 @@ __device__ __forceinline__ void gemm_tc_body(const TcArgs &a) {
             // tile; then this warp drains the previous tile's accumulator, then continues
             const int64_t g0 = gs, r0 = gr;
             int t = grp;
-            const int prefill = kTcAStages;  // stages of this tile (both groups) before the epilogue
+            const int prefill = kTcAStages;  // stages of this tile (all groups) before the epilogue
             const int64_t row0 = tile_rows(tile);
             const int nk = tile_nk(tile), kb0 = tile_kb0(tile);
-            for (; t < nk && t < prefill && ok; t += 2)
+            for (; t < nk && t < prefill && ok; t += kTcDqGroups)
                 ok = dequant_stage(g0 + t, r0 + (t >> 1), kb0 + (t >> 1), row0);
             if (ok && prev_tile >= 0) ok = epilogue(prev_tile, it - 1);
-            for (; t < nk && ok; t += 2) ok = dequant_stage(g0 + t, r0 + (t >> 1), kb0 + (t >> 1), row0);
+            for (; t < nk && ok; t += kTcDqGroups) ok = dequant_stage(g0 + t, r0 + (t >> 1), kb0 + (t >> 1), row0);
             gs += nk;
             gr += tile_kb1(tile) - kb0;
             prev_tile = tile;
