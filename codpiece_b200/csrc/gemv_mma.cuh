@@ -196,10 +196,17 @@ __device__ __forceinline__ void q4k_superblock(const uint8_t *p0, const uint8_t 
     for (int ng = 0; ng < NG; ng++)
 #pragma unroll
         for (int i = 0; i < 4; i++) ilo[ng][i] = ihi[ng][i] = 0;
+    // the superblock's quant fragments of both rows first (M = 16: 90.4 -> 87.6 us for the FFN set)
+    uint2 qq0[4], qq1[4];
 #pragma unroll
     for (int jj = 0; jj < 4; jj++) {
-        const uint2 q0 = *reinterpret_cast<const uint2 *>(p0 + 16 + 32 * jj + 8 * tig);
-        const uint2 q1 = *reinterpret_cast<const uint2 *>(p1 + 16 + 32 * jj + 8 * tig);
+        qq0[jj] = *reinterpret_cast<const uint2 *>(p0 + 16 + 32 * jj + 8 * tig);
+        qq1[jj] = *reinterpret_cast<const uint2 *>(p1 + 16 + 32 * jj + 8 * tig);
+    }
+#pragma unroll
+    for (int jj = 0; jj < 4; jj++) {
+        const uint2 q0 = qq0[jj];
+        const uint2 q1 = qq1[jj];
         constexpr uint32_t M4 = 0x0f0f0f0fu, H4 = 0xf0f0f0f0u;
         const uint32_t sw0 = jj < 2 ? sc0a : sc0b, sw1 = jj < 2 ? sc1a : sc1b;
         const int sl0 = byte_of(sw0, (2 * jj) & 3), sh0 = byte_of(sw0, (2 * jj + 1) & 3);
