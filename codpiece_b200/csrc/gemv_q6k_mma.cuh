@@ -172,8 +172,10 @@ __device__ __forceinline__ void q6m_superblock(const uint8_t *tile, int rowb, in
         const int s0 = sbyte(u4_word(sca, g >> 2), g & 3), s1 = sbyte(u4_word(scbb, g >> 2), g & 3);
         isum[0] += s0 * cc[0];
         isum[1] += s1 * cc[1];
-        isum[2] += s0 * cc[2];
-        isum[3] += s1 * cc[3];
+        if (MT > 8) {  // tokens gid + 8 (zero rows of A for M <= 8)
+            isum[2] += s0 * cc[2];
+            isum[3] += s1 * cc[3];
+        }
     }
     // sum_g s_g * bsum_g for the -32 offset: bsum bytes (16 groups = k) x scales
     const int bo = b * 16 + 4 * tig;
@@ -187,8 +189,10 @@ __device__ __forceinline__ void q6m_superblock(const uint8_t *tile, int rowb, in
     const float dx0 = xd[gid * nbk + b], dx1 = MT > 8 ? xd[(gid + 8) * nbk + b] : 0.0f;
     acc[0] += (dwa * dx0) * float(isum[0] - 32 * (cl[0] + 256 * ch[0]));
     acc[1] += (dwb * dx0) * float(isum[1] - 32 * (cl[1] + 256 * ch[1]));
-    acc[2] += (dwa * dx1) * float(isum[2] - 32 * (cl[2] + 256 * ch[2]));
-    acc[3] += (dwb * dx1) * float(isum[3] - 32 * (cl[3] + 256 * ch[3]));
+    if (MT > 8) {
+        acc[2] += (dwa * dx1) * float(isum[2] - 32 * (cl[2] + 256 * ch[2]));
+        acc[3] += (dwb * dx1) * float(isum[3] - 32 * (cl[3] + 256 * ch[3]));
+    }
 }
 
 template <int MT>
