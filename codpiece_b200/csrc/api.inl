@@ -1005,6 +1005,9 @@ static cpq_status mul_mat_core(const cpq_tensor *const *w, cpq_tensor *const *y,
     if (pro.mode == CPQ_PRO_SWIGLU && !pro.r) return fail(CPQ_ERR_INVALID_ARG, "SWIGLU prologue needs r (up)");
     if ((pro.r && !aligned(pro.r, 16)) || (pro.h_out && !aligned(pro.h_out, 16)))
         return fail(CPQ_ERR_UNSUPPORTED, "prologue r/h_out must be 16-byte aligned");
+    // every CTA of a row reads the whole row for its RMS while others store x + r
+    if (pro.h_out && x && (pro.h_out == x->data || pro.h_out == pro.r))
+        return fail(CPQ_ERR_INVALID_ARG, "prologue h_out must not alias X or r");
     if (n_w < 1 || n_w > kMaxMulti) return fail(CPQ_ERR_INVALID_ARG, "n_w=%d must be in 1..%d", n_w, kMaxMulti);
     if (!w || !y) return fail(CPQ_ERR_INVALID_ARG, "weight/output arrays are null");
     MMShape s0;

@@ -166,6 +166,10 @@ def test_unsupported_and_invalid_are_reported_not_fatal(cuda):
     assert L.cpq_mul_mat(C.byref(bad), C.byref(xd), C.byref(yd), st) == 2
     assert L.cpq_mul_mat_ws(C.byref(wd), C.byref(xd), C.byref(yd), None, 0, st) == 3
     assert b"workspace" in L.cpq_last_error() or b"cpq_init" in L.cpq_last_error()
+    # the RMS prologue's residual output may not overwrite its input
+    xa = cuda.randn(8, 512, device="cuda")
+    with pytest.raises(_lib.CpqError, match="alias"):
+        mm.mul_mat_fused([w], xa, mode=mm.PRO_RMS, h_out=xa)
     # and a valid call still works afterwards
     assert L.cpq_mul_mat(C.byref(wd), C.byref(xd), C.byref(yd), C.c_void_p(cuda.cuda.current_stream().cuda_stream)) == 0
     cuda.cuda.synchronize()
