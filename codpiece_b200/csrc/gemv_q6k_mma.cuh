@@ -15,17 +15,21 @@
 // Tiles. A tile is 8 consecutive weight rows over the whole K: 8 * K/256 *
 // 210 bytes, a multiple of 16 whatever the row alignment, fetched by one bulk
 // copy into a ring of q6m_stages() tile slots shared by the CTA. For M <= 8
-// the CTA has two teams of 8 warps taking alternate tiles (two warps per
-// scheduler are too few to hide the latency of this kernel's long dependent
-// chains); the ring then has an even number of slots, so the previous tile in
-// a slot always belongs to the same team, whose warps have waited for it: a
-// wait on a slot's barrier is never two phases behind. For M <= 16 the larger
-// activations leave room for three slots and one team. In a team,
-// warp w takes superblocks [w*nbk/8, (w+1)*nbk/8) of the tile and leaves its
-// fp32 partial [16 tokens][8 rows] in a per-slot buffer; the last warp to
-// arrive (shared-memory counter) adds the 8 partials in warp order, stores the
-// rows and refills the slot with the tile kQ6mStages ahead. CTAs take
-// contiguous ranges of tiles.
+// the CTA has two teams of W = 10 warps taking alternate tiles (fewer warps
+// per scheduler are too few to hide the latency of this kernel's long
+// dependent chains); the ring then has an even number of slots, so the
+// previous tile in a slot always belongs to the same team, whose warps have
+// waited for it: a wait on a slot's barrier is never two phases behind. For
+// M <= 16 the larger activations leave room for three slots and one team of
+// W = 10. In a team, warp w takes superblocks [w*nbk/W, (w+1)*nbk/W) of the
+// tile (two each at K = 5120; with 8 warps some took three, which set the
+// tile's time: head at M = 4 / 8 / 16 232 / 234 / 330 -> 204 / 207 / 312 us)
+// and leaves its fp32 partial [16 tokens][8 rows] in a per-slot buffer; the
+// last warp to arrive (shared-memory counter) adds the W partials in warp
+// order, stores the rows and refills the slot with the tile q6m_stages()
+// ahead. CTAs take contiguous ranges of tiles. The M <= 8 instance runs 640
+// threads (at most 102 registers: a few bytes spill, measured cheaper than 8
+// warps without spills).
 //
 // Activations in shared memory (copied once per CTA from the quantizer's
 // image): quants per token row (row stride K + 64 bytes), inside each
@@ -40,9 +44,16 @@
 
 namespace cpq {
 
-constexpr int kQ6mWarps = 8;   // warps of a team (one tile)
+#ifndef CPQ_Q6M_WARPS8
+#define CPQ_Q6M_WARPS8 10
+#endif
+#ifndef CPQ_Q6M_WARPS16
+#define CPQ_Q6M_WARPS16 10
+#endif
+// warps of a team (one tile): CPQ_Q6M_WARPS8 for M <= 8 (two teams), CPQ_Q6M_WARPS16 for M <= 16 (one team)
+__host__ __device__ constexpr int q6m_warps(int mt) { return mt <= 8 ? CPQ_Q6M_WARPS8 : CPQ_Q6M_WARPS16; }
 __host__ __device__ constexpr int q6m_teams(int mt) { return mt <= 8 ? 2 : 1; }
-__host__ __device__ constexpr int q6m_threads(int mt) { return kQ6mWarps * q6m_teams(mt) * 32; }
+__host__ __device__ constexpr int q6m_threads(int mt) { return q6m_warps(mt) * q6m_teams(mt) * 32; }
 constexpr int kQ6mMaxK = 30 * kQK_K;  // 8 rows x 30 superblocks = 50,400 B per tile
 __host__ __device__ constexpr int q6m_stages(int mt) { return mt <= 8 ? 4 : 3; }
 static_assert(q6m_stages(8) % 2 == 0, "two teams need an even ring");
@@ -52,9 +63,10 @@ __host__ __device__ constexpr int q6m_act_bytes(int nbk, int mt) {
     return int(align_up(size_t(mt) * q6m_qs_stride(nbk), 16) + 2 * align_up(size_t(mt) * nbk * 16, 16) +
                align_up(size_t(mt) * nbk * 4, 16));
 }
-constexpr int kQ6mRedBytes = kQ6mWarps * 16 * 8 * 4;  // one slot: [warp][16 tokens][8 rows] fp32
+// one slot of partials: [warp][16 tokens][8 rows] fp32
+__host__ __device__ constexpr int q6m_red_bytes(int mt) { return q6m_warps(mt) * 16 * 8 * 4; }
 __host__ __device__ constexpr int q6m_smem_bytes(int nbk, int mt) {
-    return 256 + q6m_act_bytes(nbk, mt) + q6m_stages(mt) * (q6m_tile_bytes(nbk) + kQ6mRedBytes) + 16;
+    return 256 + q6m_act_bytes(nbk, mt) + q6m_stages(mt) * (q6m_tile_bytes(nbk) + q6m_red_bytes(mt)) + 16;
 }
 
 struct Q6MmaArgs {
@@ -199,6 +211,7 @@ template <int MT>
 __global__ void __launch_bounds__(q6m_threads(MT), 1) gemv_q6k_mma_kernel(const __grid_constant__ Q6MmaArgs a) {
     constexpr int S = q6m_stages(MT);
     extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int kQ6mWarps = q6m_warps(MT);
     const int lane = threadIdx.x & 31, team = int(threadIdx.x >> 5) / kQ6mWarps, warp = int(threadIdx.x >> 5) % kQ6mWarps;
     const int gid = lane >> 2, tig = lane & 3;
     const int nbk = a.nbk;
